@@ -1,0 +1,423 @@
+"""Benchmark of the B200 FP16 GEMM (the path behind the reference's `solve`).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--M 8192 --N 8192 --K 8192] [--chunks C]
+
+Workload: FP16 GEMM C = A @ B (alpha=1, beta=0), row-major, A/B full-entropy U[-1,1) from the
+reference benchmark's counter-hash fill (three_way.cu:22-33, seeds three_way.cu:71-72).
+One step = one GEMM launch. At N=1 the shape is 8192^3, the configuration the metric is quoted
+on. With N GPUs (torchrun, one process per GPU) the job is the row-sharded GEMM of
+BASELINE configs[4]'s scheme at fixed per-GPU work: M = 8192*N rows split by rank, B
+replicated, and the C row blocks all-gathered over NCCL inside every step (weak scaling).
+
+Timing follows the reference methodology (three_way.cu): L2 flushed (memset of 3x the L2
+size) before every timed launch, one launch between two CUDA events on the launching stream,
+cuBLAS cublasGemmEx timed interleaved on the same data; W >= 3 warm-up steps; K timed
+steps bracketed by barrier + synchronize; the max over ranks. `value` = whole-job TFLOPS over
+the K steps; `e2e` = the same metric through the C ABI (`solve` at N=1) with host buffers
+(pinned H2D of A and B, D2H of C inside the timed region).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_PEAK_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--M", type=int, default=8192, help="rows per GPU")
+    ap.add_argument("--N", type=int, default=8192)
+    ap.add_argument("--K", type=int, default=8192)
+    ap.add_argument("--chunks", type=int, default=1, help="row chunks for gather overlap (N>1)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(M, N, K):
+    """dram bytes per launch from the committed ncu summary for this kernel and shape."""
+    path = os.path.join(ROOT, "profiles", "hgemm_tc_kernel_8192x8192x8192.md")
+    if (M, N, K) != (8192, 8192, 8192) or not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx = [], None
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def hash_fill_(t, seed):
+    """three_way.cu:22-33 counter-hash fill, computed on the device with torch int64 ops."""
+    import torch
+    flat = t.view(-1)
+    n = flat.numel()
+    step = 1 << 25
+    m32 = 0xFFFFFFFF
+    for b in range(0, n, step):
+        e = min(n, b + step)
+        i = torch.arange(b, e, device=t.device, dtype=torch.int64)
+        h = ((i * 2654435761) & m32) ^ (seed & m32)
+        h ^= h >> 15
+        h = (h * 2246822519) & m32
+        h ^= h >> 13
+        h = (h * 3266489917) & m32
+        h ^= h >> 16
+        flat[b:e] = ((h & 0xFFFF).to(torch.float32) / 32768.0 - 1.0).to(torch.float16)
+    return t
+
+
+def cpu_baseline(M, N, K, budget_s=10.0):
+    """The oracle (restated reference fp64 GEMM) on a bounded row sample of the workload,
+    all host threads; TFLOPS of the sample."""
+    import numpy as np
+    from oracle import oracle as orc
+    orc.build()
+    threads = orc.max_threads()
+    B = orc.hash_fill_half((K, N), 0x85EBCA6B)
+    rows_probe = 4
+    A = orc.hash_fill_half((rows_probe, K), 0x9E3779B9)
+    t0 = time.perf_counter()
+    orc.gemm_f64(A, B, rows=np.arange(rows_probe), threads=threads)
+    dt = time.perf_counter() - t0
+    rows = int(max(threads, min(M, rows_probe * budget_s / max(dt, 1e-6))))
+    rows = max(threads, (rows // threads) * threads)
+    A = orc.hash_fill_half((rows, K), 0x9E3779B9)
+    t0 = time.perf_counter()
+    orc.gemm_f64(A, B, rows=np.arange(rows), threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": "TFLOPS", "cores": threads,
+            "kind": "port",
+            "sample": f"rows 0..{rows - 1} of the {M}x{N}x{K} GEMM ({rows}x{N}x{K} MACs), "
+                      f"fp64 accumulate in k order (check_fp64.cu:39-44), {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU implementation of the path (the fp64 host GEMM
+    of check_fp64.cu:39-44, restated in oracle/ because the reference's own file cannot run
+    without an sm_90 GPU), timed on this box's host cores over bounded samples."""
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle as orc
+    orc.build()
+    M, N, K = args.M * world, args.N, args.K
+    threads = orc.max_threads()
+    B = orc.hash_fill_half((K, N), 0x85EBCA6B)
+    rows = max(threads, 2 * threads)
+    A = orc.hash_fill_half((rows, K), 0x9E3779B9)
+    for _ in range(max(args.warmup, 0)):
+        orc.gemm_f64(A, B, rows=np.arange(threads), threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        orc.gemm_f64(A, B, rows=np.arange(rows), threads=threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = 2.0 * rows * N * K * len(times) / total / 1e12
+    sample = f"{rows} rows of the {M}x{N}x{K} GEMM per step ({rows}x{N}x{K} MACs, fp64)"
+    print(json.dumps({
+        "impl": "reference", "metric": "fp16_gemm_tflops", "value": value, "unit": "TFLOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"gemm_{M}x{N}x{K}_rowsharded" if world > 1 else f"gemm_{M}x{N}x{K}",
+                   "alpha": 1.0, "beta": 0.0},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
+def main():
+    args = parse()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import hopper_gemm_b200 as hg
+    from hopper_gemm_b200._native import cublas_ref_lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=120))
+
+    Ml, N, K = args.M, args.N, args.K
+    M = Ml * world
+    flops_job = 2.0 * M * N * K
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    A = hash_fill_(torch.empty((Ml, K), dtype=torch.float16, device=dev), 0x9E3779B9 ^ rank)
+    B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device=dev), 0x85EBCA6B)
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    R = torch.empty((Ml, N), dtype=torch.float16, device=dev)  # cuBLAS output
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    flush = torch.empty(3 * l2, dtype=torch.uint8, device=dev)
+
+    comm = None
+    if world > 1:
+        import ctypes
+        idbuf = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            host_id = (ctypes.c_ubyte * 128)()
+            st = hg.lib.hgemm_comm_unique_id(host_id, 128)
+            assert st == 0, hg.status_string(st)
+            idbuf.copy_(torch.tensor(list(host_id), dtype=torch.uint8))
+        dist.broadcast(idbuf, 0)
+        id_bytes = bytes(idbuf.cpu().tolist())
+        comm_p = ctypes.c_void_p()
+        st = hg.lib.hgemm_comm_init(ctypes.byref(comm_p), world, id_bytes, 128, rank)
+        assert st == 0, hg.status_string(st)
+        comm = comm_p
+
+    def ours():
+        if comm is None:
+            st = hg.lib.hgemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), Ml, N, K, 1.0,
+                                     0.0, sptr)
+        else:
+            st = hg.lib.hgemm_sharded_rank(comm, A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N,
+                                           K, 1.0, 0.0, args.chunks, sptr)
+        if st != 0:
+            raise RuntimeError(hg.status_string(st))
+
+    cub = cublas_ref_lib()
+
+    def cublas():
+        st = cub.hgemm_cublas_ref(A.data_ptr(), B.data_ptr(), R.data_ptr(), Ml, N, K, 1.0, 0.0,
+                                  sptr)
+        if st != 0:
+            raise RuntimeError("cublas failed")
+
+    def sample(fn):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        flush.fill_(0x5A)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        return e0, e1
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up (interleaved, as three_way.cu:141)
+    for _ in range(args.warmup):
+        ours()
+        cublas()
+    barrier()
+
+    # timed region: K steps of ours, cuBLAS interleaved round-robin
+    ev_ours, ev_cub = [], []
+    region0 = torch.cuda.Event(enable_timing=True)
+    region1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        region0.record(stream)
+        for _ in range(args.steps):
+            ev_ours.append(sample(ours))
+            ev_cub.append(sample(cublas))
+        region1.record(stream)
+        barrier()
+    t_ours = [a.elapsed_time(b) for a, b in ev_ours]
+    t_cub = [a.elapsed_time(b) for a, b in ev_cub]
+    region_ms = region0.elapsed_time(region1)
+    tot = torch.tensor([sum(t_ours), sum(t_cub)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    ms_ours = float(tot[0]) / args.steps
+    ms_cub = float(tot[1]) / args.steps
+    value = flops_job / (ms_ours * 1e-3) / 1e12
+    cub_value = flops_job / world * world / (ms_cub * 1e-3) / 1e12 if world == 1 else None
+    ratios = [c / o for o, c in zip(t_ours, t_cub)]
+
+    # correctness spot check of the benchmarked output against cuBLAS
+    torch.cuda.synchronize()
+    rb = hg.shard_rows(M, world, rank)[0]
+    mine = C[rb:rb + Ml].float()
+    spot_l2 = float((mine - R.float()).norm() / R.float().norm())
+
+    # end to end through the C ABI with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hA = torch.empty((Ml, K), dtype=torch.float16, pin_memory=True)
+        hB = torch.empty((K, N), dtype=torch.float16, pin_memory=True)
+        hC = torch.empty((Ml, N), dtype=torch.float16, pin_memory=True)
+        hA.copy_(A)
+        hB.copy_(B)
+        dA2 = torch.empty_like(A)
+        dB2 = torch.empty_like(B)
+        e2e_steps = max(3, min(args.steps, 10))
+
+        def e2e_step():
+            dA2.copy_(hA, non_blocking=True)
+            dB2.copy_(hB, non_blocking=True)
+            if comm is None:
+                hg.lib.solve(dA2.data_ptr(), dB2.data_ptr(), C.data_ptr(), Ml, N, K, 1.0, 0.0)
+            else:
+                st = hg.lib.hgemm_sharded_rank(comm, dA2.data_ptr(), dB2.data_ptr(),
+                                               C.data_ptr(), M, N, K, 1.0, 0.0, args.chunks,
+                                               sptr)
+                assert st == 0
+            hC.copy_(C[rb:rb + Ml], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0]) / e2e_steps
+        e2e = {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+               "h2d_bytes_per_step": 2 * (Ml * K + K * N), "d2h_bytes_per_step": 2 * Ml * N,
+               "ms_per_step": e2e_ms,
+               "path": "solve() C ABI, pinned host buffers" if comm is None else
+                       "hgemm_sharded_rank() C ABI, pinned host buffers"}
+        assert hg.last_status() == 0, hg.status_string(hg.last_status())
+
+    st_dev, where = hg.device_status(clear=False)
+    if comm is not None:
+        hg.lib.hgemm_comm_destroy(comm)
+
+    if rank == 0:
+        peak, hbm, src = peaks()
+        achieved = 2.0 * Ml * N * K / (ms_ours * 1e-3) / 1e12 if world == 1 else \
+            2.0 * Ml * N * K / (statistics.mean(t_ours) * 1e-3) / 1e12
+        traffic = profiled_traffic(Ml, N, K)
+        line = {
+            "metric": "fp16_gemm_tflops", "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_ours,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (three_way.cu counter-hash fill, U[-1,1))",
+            "config": {"workload": (f"gemm_{M}x{N}x{K}" if world == 1 else
+                                    f"gemm_{M}x{N}x{K}_rowsharded_allgather"),
+                       "M": M, "N": N, "K": K, "alpha": 1.0, "beta": 0.0,
+                       "rows_per_gpu": Ml, "parallelism": f"rowshard{world}",
+                       "l2": "flushed (3x L2 memset) before every timed launch",
+                       "timing": "CUDA events around each launch on the launching stream"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{src} bf16 dense (burst)"},
+            "cublas": {"value": cub_value, "ms_per_step": ms_cub,
+                       "paired_ratio_median": statistics.median(ratios) if ratios else None,
+                       "call": "cublasGemmEx(CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT)"},
+            "median_ms": statistics.median(t_ours),
+            "region_ms_incl_flush_and_cublas": region_ms,
+            "check_rel_l2_vs_cublas": spot_l2,
+            "device_status": st_dev,
+            "e2e": e2e,
+            "gpu_launches": args.steps * (1 if comm is None else max(1, args.chunks)),
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(Ml, N, K)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

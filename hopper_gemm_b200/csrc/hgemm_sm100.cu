@@ -1,0 +1,1119 @@
+// B200 (sm_100a) FP16 GEMM: C = alpha * A[M,K] @ B[K,N] + beta * C, row-major, half in/out,
+// fp32 accumulate. Kernel, per-shape dispatcher and the C ABI declared in hgemm_b200.h.
+//
+// Design (B200-first, not a translation of the reference's sm_90a wgmma kernel):
+//   * Persistent grid, one CTA per SM (~226 KB of shared memory each), optionally launched
+//     as 2-CTA clusters that act as one UMMA pair: `tcgen05.mma.cta_group::2` computes a
+//     256 x BN tile, each CTA holding 128 rows of A and BN/2 columns of B in its own smem.
+//     The pair shares B through the tensor core, which is what the reference bought with a
+//     TMA multicast of B (mma_half.cu:331-367). No multicast load is issued anywhere.
+//   * Warp roles: warp 0 = TMA producer (one lane), warp 1 = TMEM allocator + UMMA issuer
+//     (one lane of the pair's leader CTA), warps 2..5 = epilogue (TMEM lane quarters).
+//   * fp32 accumulators live in TMEM, double buffered (2 x BN columns), so the epilogue of
+//     tile i overlaps the mainloop of tile i+1.
+//   * A is consumed K-major and B N-major straight from the caller's row-major buffers;
+//     both arrive through 128-byte-swizzled TMA boxes (64 halves wide). TMA zero-fills
+//     out-of-range rows/columns, which handles every ragged M/N/K edge.
+//   * Epilogue: tcgen05.ld -> alpha*acc (+ beta*C_in) in fp32 -> one RNE to half ->
+//     128B-swizzled smem staging -> TMA store (N % 8 == 0), or coalesced predicated stores
+//     when C's row stride is not 16-byte aligned (N % 8 != 0).
+//   * Every wait is bounded (globaltimer); a wait that runs out records a device status
+//     word, raises the CTA's abort flag and the kernel unwinds, freeing its TMEM.
+//
+// Reference correspondence (yz-wqf/Hopper_GEMM, mma_half.cu):
+//   gemm_kernel 887-1222 -> hgemm_tc_kernel; store_c_tile(_tma) 724-872 -> epilogue below;
+//   gemm_fallback 1225-1250 -> hgemm_simt_kernel; pad_copy_kernel 1254-1261 ->
+//   restride_kernel; make_tensor_map/get_encode_tiled 1264-1297 -> encode_2d;
+//   tma_compatible 1301-1306 / pad_workspace 1308-1322 / launch 1530-1563 -> launch_impl;
+//   launch_mainloop 1441-1526 -> make_plan; autotune 1570-1628 -> hgemm_launch_tuned;
+//   solve 1636-1640 -> solve.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
+
+#include "hgemm_b200.h"
+#include "ptx_sm100.cuh"
+
+namespace hgemm {
+
+// ============================================================================ constants
+constexpr int BK = 64;          // k per pipeline stage: one 128-byte swizzle row of halves
+constexpr int CTA_M = 128;      // accumulator rows per CTA (= TMEM lanes)
+constexpr int UMMA_K = 16;      // k per tcgen05.mma.kind::f16
+constexpr int EPI_ROWS = 32;    // rows per epilogue warp (its TMEM lane quarter)
+constexpr int EPI_COLS = 64;    // columns per epilogue chunk (one 128-byte swizzle row)
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in dynamic shared memory per block
+constexpr int BAR_BYTES = 256;
+
+// Device status word: 0, or kDevTimeout | where. Written once per failure (first wins).
+constexpr unsigned kDevTimeout = 0x100u;
+enum WaitSite : unsigned {
+  kSiteProducerEmpty = 1,
+  kSiteMmaTmemEmpty = 2,
+  kSiteMmaFull = 3,
+  kSiteEpiTmemFull = 4,
+  kSiteDrain = 5,
+  kSiteSelftest = 6,
+};
+__device__ unsigned int g_dev_status = 0;
+
+template <int PAIR, int BN>
+struct TileCfg {
+  static constexpr int B_COLS = BN / PAIR;  // B columns this CTA loads
+  static constexpr int B_BOXES = B_COLS / 64;
+  static constexpr int A_BYTES = CTA_M * BK * 2;  // 16 KB
+  static constexpr int B_BYTES = B_COLS * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TX_BYTES = STAGE_BYTES * PAIR;  // armed on the leader's barrier
+  static constexpr int EPI_BYTES = 4 * 2 * EPI_ROWS * 128;  // 4 warps x 2 buffers x 4 KB
+  static constexpr int STAGES_FIT = (SMEM_LIMIT - EPI_BYTES - 1024 - BAR_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers
+  static constexpr int UMMA_M = CTA_M * PAIR;
+  static_assert(B_COLS % 64 == 0, "B slice must be whole 64-column swizzle blocks");
+  static_assert(STAGES >= 3, "pipeline too shallow");
+  static_assert(SMEM <= SMEM_LIMIT, "shared memory over budget");
+  static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0,
+                "TMEM allocation must be a power of two in [32, 512]");
+  static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
+};
+
+struct KParams {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles, num_kb;
+  int group_m;
+  float alpha, beta;
+  __half *C;
+  unsigned long long timeout_ns;
+};
+
+// ============================================================================ device helpers
+struct WaitCtx {
+  volatile int *abort_flag;     // this CTA's flag (generic pointer to smem)
+  uint32_t peer_abort;          // shared::cluster address of the peer's flag (pair), or 0
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ void raise_abort(const WaitCtx &w, unsigned where) {
+  atomicCAS(&g_dev_status, 0u, kDevTimeout | where);
+  *w.abort_flag = 1;
+  if (w.peer_abort)
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(w.peer_abort), "r"(1) : "memory");
+}
+
+// Bounded mbarrier wait. Returns false if the CTA is aborting or the wait timed out.
+template <bool CLUSTER_ACQ>
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const WaitCtx &w,
+                                         unsigned where) {
+  auto probe = [&]() {
+    return CLUSTER_ACQ ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity);
+  };
+  if (probe()) return true;
+  const uint64_t t0 = ptx::globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (probe()) return true;
+    if ((n & 15u) == 0) {
+      if (*w.abort_flag) return false;
+      if (ptx::globaltimer() - t0 > w.timeout_ns) {
+        raise_abort(w, where);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void decode_tile(int t, const KParams &p, int &tm, int &tn) {
+  // Bands of group_m tile-rows; inside a band the M index runs fastest, so the CTAs working
+  // at the same time share a few A row-blocks and B column-blocks in L2.
+  const int band_tiles = p.group_m * p.tiles_n;
+  const int band = t / band_tiles;
+  const int idx = t - band * band_tiles;
+  const int m0 = band * p.group_m;
+  const int rows = min(p.group_m, p.tiles_m - m0);
+  tm = m0 + idx % rows;
+  tn = idx / rows;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Offset of 16-byte chunk j of row r inside a 128B-swizzled 1024-byte-aligned buffer whose
+// rows are 128 bytes: the chunk index is XORed with r mod 8 (TMA SWIZZLE_128B pattern).
+__device__ __forceinline__ uint32_t sw128_off(int r, int j) {
+  return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// ============================================================================ the kernel
+template <int PAIR, int BN, bool TMA_EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    hgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const KParams p) {
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
+  using Cfg = TileCfg<PAIR, BN>;
+  constexpr int S = Cfg::STAGES;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  const uint32_t sA0 = base;
+  const uint32_t sB0 = base + S * Cfg::A_BYTES;
+  uint8_t *epi = smem + S * Cfg::STAGE_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(epi + Cfg::EPI_BYTES);
+  uint64_t *full = bars;             // [S]   TMA bytes landed (leader CTA's copy is used)
+  uint64_t *empty = bars + S;        // [S]   UMMA finished reading the stage
+  uint64_t *tfull = bars + 2 * S;    // [2]   accumulator buffer ready for the epilogue
+  uint64_t *tempty = bars + 2 * S + 2;  // [2] epilogue drained the accumulator buffer
+  uint64_t *drain = bars + 2 * S + 4;   // [1] teardown: all issued UMMAs retired
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = (PAIR == 2) ? ptx::cluster_ctarank() : 0u;
+  const int cid = (PAIR == 2) ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int ncl = (PAIR == 2) ? static_cast<int>(ptx::nclusters_x()) : static_cast<int>(gridDim.x);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(ptx::smem_u32(&tfull[a]), 1);
+      ptx::mbar_init(ptx::smem_u32(&tempty[a]), 4 * PAIR);
+    }
+    ptx::mbar_init(ptx::smem_u32(drain), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init_cluster();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+    if (TMA_EPI) ptx::prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc<PAIR>(ptx::smem_u32(tmem_holder), Cfg::TMEM_COLS);
+    ptx::tmem_relinquish<PAIR>();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (PAIR == 2) ptx::cluster_sync();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_holder);
+
+  WaitCtx wctx;
+  wctx.abort_flag = abort_flag;
+  wctx.peer_abort = (PAIR == 2) ? ptx::mapa(ptx::smem_u32(const_cast<int *>(abort_flag)), rank ^ 1u) : 0u;
+  wctx.timeout_ns = p.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      long long issued = 0;
+      const uint32_t full_leader0 =
+          (PAIR == 2) ? ptx::mapa(ptx::smem_u32(&full[0]), 0u) : ptx::smem_u32(&full[0]);
+      bool ok = true;
+      for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+        int tm, tn;
+        decode_tile(t, p, tm, tn);
+        const int arow = tm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M;
+        const int bcol = tn * BN + static_cast<int>(rank) * Cfg::B_COLS;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!wait_bar<false>(ptx::smem_u32(&empty[s]), ph ^ 1u, wctx, kSiteProducerEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fbar = full_leader0 + static_cast<uint32_t>(s) * 8u;
+          if (rank == 0) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&full[s]), Cfg::TX_BYTES);
+          const uint32_t dA = sA0 + static_cast<uint32_t>(s) * Cfg::A_BYTES;
+          const uint32_t dB = sB0 + static_cast<uint32_t>(s) * Cfg::B_BYTES;
+          if (PAIR == 2) {
+            ptx::tma_load_2d_pair(&tmA, dA, fbar, kb * BK, arow);
+#pragma unroll
+            for (int b = 0; b < Cfg::B_BOXES; ++b)
+              ptx::tma_load_2d_pair(&tmB, dB + b * (BK * 128), fbar, bcol + 64 * b, kb * BK);
+          } else {
+            ptx::tma_load_2d(&tmA, dA, fbar, kb * BK, arow);
+#pragma unroll
+            for (int b = 0; b < Cfg::B_BOXES; ++b)
+              ptx::tma_load_2d(&tmB, dB + b * (BK * 128), fbar, bcol + 64 * b, kb * BK);
+          }
+          ++issued;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Unwinding: let the loads this CTA armed land before the CTA can exit.
+        const int armed = issued >= S ? S : static_cast<int>(issued);
+        for (int j = 0; j < armed; ++j) {
+          const uint32_t par = (j < s) ? ph : (ph ^ 1u);
+          WaitCtx dctx = wctx;
+          volatile int no_abort = 0;
+          dctx.abort_flag = &no_abort;
+          dctx.peer_abort = 0;
+          dctx.timeout_ns = 50000000ull;
+          if (!wait_bar<false>(ptx::smem_u32(&full[j]), par, dctx, kSiteDrain)) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ UMMA issuer
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = ptx::umma_idesc_f16_f32(Cfg::UMMA_M, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool issued_any = false;
+      bool ok = true;
+      for (int t = cid; t < p.num_tiles && ok; t += ncl, ++it) {
+        const int acc = it & 1;
+        const uint32_t aph = static_cast<uint32_t>(it >> 1) & 1u;
+        if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[acc]), aph ^ 1u, wctx, kSiteMmaTmemEmpty)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t dtm = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint64_t adesc = ptx::umma_desc_sw128(sA0 + s * Cfg::A_BYTES, 16, 1024);
+          const uint64_t bdesc = ptx::umma_desc_sw128(sB0 + s * Cfg::B_BYTES, BK * 128, 1024);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            // A (K-major): +32 bytes per k16 inside the swizzle row. B (N-major): +16 rows
+            // of 128 bytes per k16. Descriptor start addresses are in 16-byte units.
+            ptx::umma_f16<PAIR>(dtm, adesc + static_cast<uint64_t>(2 * k),
+                                bdesc + static_cast<uint64_t>(128 * k), idesc,
+                                (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          const uint32_t eb = ptx::smem_u32(&empty[s]);
+          if (PAIR == 2)
+            ptx::umma_commit_pair_mask(eb, 0x3);  // both CTAs' copies of empty[s]
+          else
+            ptx::umma_commit<1>(eb);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t fb = ptx::smem_u32(&tfull[acc]);
+        if (PAIR == 2)
+          ptx::umma_commit_pair_mask(fb, 0x3);
+        else
+          ptx::umma_commit<1>(fb);
+      }
+      if (!ok && issued_any) {
+        // Unwinding: every UMMA this thread issued must retire before TMEM is freed.
+        ptx::umma_commit<PAIR>(ptx::smem_u32(drain));
+        WaitCtx dctx = wctx;
+        volatile int no_abort = 0;
+        dctx.abort_flag = &no_abort;
+        dctx.peer_abort = 0;
+        dctx.timeout_ns = 50000000ull;
+        wait_bar<false>(ptx::smem_u32(drain), 0u, dctx, kSiteDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue warps
+    const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are the ones this warp may read
+    uint8_t *stg0 = epi + q * (2 * EPI_ROWS * 128);
+    const uint32_t tempty_leader =
+        (PAIR == 2) ? ptx::mapa(ptx::smem_u32(&tempty[0]), 0u) : ptx::smem_u32(&tempty[0]);
+    const float alpha = p.alpha, beta = p.beta;
+    int it = 0;
+    int chunk_ctr = 0;
+    for (int t = cid; t < p.num_tiles; t += ncl, ++it) {
+      const int acc = it & 1;
+      const uint32_t aph = static_cast<uint32_t>(it >> 1) & 1u;
+      // One lane waits; the result is broadcast so the warp stays converged for the
+      // .sync.aligned TMEM loads below.
+      int ok = 1;
+      if (lane == 0)
+        ok = wait_bar<PAIR == 2>(ptx::smem_u32(&tfull[acc]), aph, wctx, kSiteEpiTmemFull) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      int tm, tn;
+      decode_tile(t, p, tm, tn);
+      const int row0 = tm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M + EPI_ROWS * q;
+      const int col0 = tn * BN;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(EPI_ROWS * q) << 16) + static_cast<uint32_t>(acc * BN);
+      const int r = row0 + lane;  // this thread's output row
+#pragma unroll 1
+      for (int c = 0; c < BN / EPI_COLS; ++c, ++chunk_ctr) {
+        uint32_t v[64];
+        ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
+                                *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        ptx::tmem_ld_wait();
+        if (c == BN / EPI_COLS - 1) {
+          // Whole accumulator read: hand the buffer back to the UMMA issuer.
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            const uint32_t tb = tempty_leader + static_cast<uint32_t>(acc) * 8u;
+            if (PAIR == 2)
+              ptx::mbar_arrive_cluster(tb);
+            else
+              ptx::mbar_arrive(tb);
+          }
+        }
+        const int ccol = col0 + c * EPI_COLS;
+        uint8_t *stg = stg0 + (chunk_ctr & 1) * (EPI_ROWS * 128);
+        float f[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) f[i] = alpha * __uint_as_float(v[i]);
+
+        if (TMA_EPI) {
+          // The TMA store that used this staging buffer two chunks ago must have read it.
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+          if (beta != 0.0f && r < p.M) {
+            const __half *crow = p.C + static_cast<long long>(r) * p.N;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int cc = ccol + 8 * j;
+              if (cc < p.N) {  // N % 8 == 0: a 16-byte group is wholly inside or outside
+                const uint4 u = *reinterpret_cast<const uint4 *>(crow + cc);
+                const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 cf = __half22float2(h[e]);
+                  f[8 * j + 2 * e] = fmaf(beta, cf.x, f[8 * j + 2 * e]);
+                  f[8 * j + 2 * e + 1] = fmaf(beta, cf.y, f[8 * j + 2 * e + 1]);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 w;
+            w.x = pack_half2(f[8 * j + 0], f[8 * j + 1]);
+            w.y = pack_half2(f[8 * j + 2], f[8 * j + 3]);
+            w.z = pack_half2(f[8 * j + 4], f[8 * j + 5]);
+            w.w = pack_half2(f[8 * j + 6], f[8 * j + 7]);
+            *reinterpret_cast<uint4 *>(stg + sw128_off(lane, j)) = w;
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < p.M && ccol < p.N) ptx::tma_store_2d(&tmC, ptx::smem_u32(stg), ccol, row0);
+            ptx::bulk_commit_group();  // one group per chunk, empty when nothing was stored
+          }
+        } else {
+          // C's rows are not 16-byte aligned: stage through smem, then coalesced 2-byte
+          // accesses (lanes along a row), predicated on the M/N edges.
+          __syncwarp();
+          __half *sh = reinterpret_cast<__half *>(stg);
+          if (beta != 0.0f) {
+#pragma unroll 1
+            for (int rr = 0; rr < EPI_ROWS; ++rr) {
+              const int gr = row0 + rr;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int cc = lane + 32 * h;
+                const int gc = ccol + cc;
+                __half val = __float2half(0.0f);
+                if (gr < p.M && gc < p.N) val = p.C[static_cast<long long>(gr) * p.N + gc];
+                sh[(sw128_off(rr, cc >> 3) >> 1) + (cc & 7)] = val;
+              }
+            }
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint4 u = *reinterpret_cast<const uint4 *>(stg + sw128_off(lane, j));
+              const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 cf = __half22float2(h[e]);
+                f[8 * j + 2 * e] = fmaf(beta, cf.x, f[8 * j + 2 * e]);
+                f[8 * j + 2 * e + 1] = fmaf(beta, cf.y, f[8 * j + 2 * e + 1]);
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 w;
+            w.x = pack_half2(f[8 * j + 0], f[8 * j + 1]);
+            w.y = pack_half2(f[8 * j + 2], f[8 * j + 3]);
+            w.z = pack_half2(f[8 * j + 4], f[8 * j + 5]);
+            w.w = pack_half2(f[8 * j + 6], f[8 * j + 7]);
+            *reinterpret_cast<uint4 *>(stg + sw128_off(lane, j)) = w;
+          }
+          __syncwarp();
+#pragma unroll 1
+          for (int rr = 0; rr < EPI_ROWS; ++rr) {
+            const int gr = row0 + rr;
+            if (gr >= p.M) break;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int cc = lane + 32 * h;
+              const int gc = ccol + cc;
+              if (gc < p.N)
+                p.C[static_cast<long long>(gr) * p.N + gc] = sh[(sw128_off(rr, cc >> 3) >> 1) + (cc & 7)];
+            }
+          }
+        }
+      }
+    }
+    if (TMA_EPI && lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------------ teardown
+  if (*abort_flag) ptx::nanosleep_ns(20000);  // unwinding: let stray copies land
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (PAIR == 2) ptx::cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc<PAIR>(tmem_base, Cfg::TMEM_COLS);
+  }
+#endif
+}
+
+// ============================================================================ other kernels
+// Scalar fallback (misaligned pointers, K == 0): 64x64 output tile per block, 4x4 per
+// thread, fp32 accumulation in increasing k, same alpha/beta/rounding rules as above.
+__global__ void __launch_bounds__(256) hgemm_simt_kernel(const __half *__restrict__ A,
+                                                         const __half *__restrict__ B,
+                                                         __half *__restrict__ C, int M, int N,
+                                                         int K, float alpha, float beta) {
+  __shared__ float sa[16][64 + 4];
+  __shared__ float sb[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int kk = i / 64, mm = i % 64;
+      const int gm = m0 + mm, gk = k0 + kk;
+      sa[kk][mm] = (gm < M && gk < K) ? __half2float(A[static_cast<long long>(gm) * K + gk]) : 0.f;
+      const int gn = n0 + mm;
+      sb[kk][mm] = (gk < K && gn < N) ? __half2float(B[static_cast<long long>(gk) * N + gn]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = sa[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = sb[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty + 16 * i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx + 16 * j;
+      if (gn >= N) continue;
+      const long long o = static_cast<long long>(gm) * N + gn;
+      float v = alpha * acc[i][j];
+      if (beta != 0.0f) v = fmaf(beta, __half2float(C[o]), v);
+      C[o] = __float2half_rn(v);
+    }
+  }
+}
+
+// Copy a rows x cols half matrix into a buffer with a 16-byte-aligned row stride `ld`
+// (ld % 8 == 0); the pad columns are written as zeros. One 16-byte store per thread step.
+__global__ void __launch_bounds__(256) restride_kernel(const __half *__restrict__ src,
+                                                       __half *__restrict__ dst, int rows,
+                                                       int cols, int ld) {
+  const long long groups_per_row = ld / 8;
+  const long long total = static_cast<long long>(rows) * groups_per_row;
+  for (long long g = blockIdx.x * 256LL + threadIdx.x; g < total; g += 256LL * gridDim.x) {
+    const int r = static_cast<int>(g / groups_per_row);
+    const int c = static_cast<int>(g - r * groups_per_row) * 8;
+    const __half *s = src + static_cast<long long>(r) * cols;
+    __align__(16) __half v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = (c + e < cols) ? s[c + e] : __float2half(0.0f);
+    *reinterpret_cast<uint4 *>(dst + static_cast<long long>(r) * ld + c) =
+        *reinterpret_cast<const uint4 *>(v);
+  }
+}
+
+// The only wait is on a barrier nothing arrives on; it must give up after `timeout_ns`.
+__global__ void wait_selftest_kernel(unsigned long long timeout_ns, int *out) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(&bar), 1);
+    flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    WaitCtx w;
+    w.abort_flag = &flag;
+    w.peer_abort = 0;
+    w.timeout_ns = timeout_ns;
+    const bool ok = wait_bar<false>(ptx::smem_u32(&bar), 0u, w, kSiteSelftest);
+    *out = ok ? HGEMM_OK : HGEMM_ERR_DEVICE_TIMEOUT;
+  }
+}
+
+// ============================================================================ host side
+namespace {
+
+thread_local int t_last_status = HGEMM_OK;
+std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+
+int set_status(int s) {
+  t_last_status = s;
+  return s;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+
+// Row-major rows x cols half matrix with row stride `ld` halves -> 2-D tensor map with a
+// box of box_rows x box_cols, 128-byte swizzle, zero fill outside the matrix.
+bool encode_2d(CUtensorMap *map, const void *ptr, int rows, int cols, long long ld, int box_rows,
+               int box_cols) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld) * sizeof(__half)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estride[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), gdim, gstride, box,
+             estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------- kernel table
+enum TileId { kT256x256 = 0, kT256x128 = 1, kT128x256 = 2, kT128x128 = 3, kT128x64 = 4, kNumTiles = 5 };
+struct TileInfo {
+  int pair, bn, stages, smem;
+};
+constexpr TileInfo kTiles[kNumTiles] = {
+    {2, 256, TileCfg<2, 256>::STAGES, TileCfg<2, 256>::SMEM},
+    {2, 128, TileCfg<2, 128>::STAGES, TileCfg<2, 128>::SMEM},
+    {1, 256, TileCfg<1, 256>::STAGES, TileCfg<1, 256>::SMEM},
+    {1, 128, TileCfg<1, 128>::STAGES, TileCfg<1, 128>::SMEM},
+    {1, 64, TileCfg<1, 64>::STAGES, TileCfg<1, 64>::SMEM},
+};
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, KParams);
+
+KernelFn kernel_for(int tile, bool tma_epi) {
+  switch (tile) {
+    case kT256x256: return tma_epi ? hgemm_tc_kernel<2, 256, true> : hgemm_tc_kernel<2, 256, false>;
+    case kT256x128: return tma_epi ? hgemm_tc_kernel<2, 128, true> : hgemm_tc_kernel<2, 128, false>;
+    case kT128x256: return tma_epi ? hgemm_tc_kernel<1, 256, true> : hgemm_tc_kernel<1, 256, false>;
+    case kT128x128: return tma_epi ? hgemm_tc_kernel<1, 128, true> : hgemm_tc_kernel<1, 128, false>;
+    default: return tma_epi ? hgemm_tc_kernel<1, 64, true> : hgemm_tc_kernel<1, 64, false>;
+  }
+}
+
+int tile_from_force(int force_bm, int force_bn) {
+  if (force_bm == 256 && force_bn == 256) return kT256x256;
+  if (force_bm == 256 && force_bn == 128) return kT256x128;
+  if (force_bm == 128 && force_bn == 256) return kT128x256;
+  if (force_bm == 128 && force_bn == 128) return kT128x128;
+  if (force_bm == 128 && force_bn == 64) return kT128x64;
+  return -1;
+}
+
+// ---------------------------------------------------------------- per-device state
+struct DevState {
+  bool init = false;
+  int sm_count = 148;
+  int cc_major = 0, cc_minor = 0;
+  int pair_slots = 74;        // co-resident 2-CTA clusters at our shared-memory size
+  bool attr_done[kNumTiles][2] = {};
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+};
+std::mutex g_mu;
+DevState g_dev[64];
+
+int current_device(int *dev) {
+  if (cudaGetDevice(dev) != cudaSuccess || *dev < 0 || *dev >= 64) return HGEMM_ERR_CUDA;
+  return HGEMM_OK;
+}
+
+// Caller holds g_mu.
+int ensure_device(int dev, DevState **out) {
+  DevState &d = g_dev[dev];
+  if (!d.init) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return HGEMM_ERR_CUDA;
+    d.sm_count = prop.multiProcessorCount;
+    d.cc_major = prop.major;
+    d.cc_minor = prop.minor;
+    d.pair_slots = d.sm_count / 2;
+    d.init = true;
+    if (d.cc_major == 10 && d.cc_minor == 0) {
+      // Co-resident clusters of two at this shared-memory size (GPC pairing may leave SMs out).
+      KernelFn k = kernel_for(kT256x256, true);
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kTiles[kT256x256].smem) == cudaSuccess) {
+        d.attr_done[kT256x256][1] = true;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * d.pair_slots, 1, 1);
+        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = kTiles[kT256x256].smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) == cudaSuccess && n > 0)
+          d.pair_slots = std::min(n, d.sm_count / 2);
+        cudaGetLastError();
+      }
+    }
+  }
+  if (d.cc_major != 10 || d.cc_minor != 0) return HGEMM_ERR_UNSUPPORTED_DEVICE;
+  *out = &d;
+  return HGEMM_OK;
+}
+
+// ---------------------------------------------------------------- planning
+int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+// Tile choice: the tile whose persistent schedule has the least per-CTA work on the
+// critical path (waves x columns per CTA), preferring the pair tiles, whose A+B traffic per
+// flop is the lowest. group_m keeps the concurrently running tiles' A and B blocks small
+// enough to stay in the 126 MB L2.
+int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int force_bn,
+              int group_m, int sm_count, int pair_slots, hgemm_plan_t *pl) {
+  std::memset(pl, 0, sizeof(*pl));
+  if (M < 0 || N < 0 || K < 0 || group_m < 0) return HGEMM_ERR_INVALID_ARG;
+  if ((force_bm != 0 || force_bn != 0) && tile_from_force(force_bm, force_bn) < 0)
+    return HGEMM_ERR_INVALID_ARG;
+  if (sm_count <= 0) sm_count = 148;
+  if (pair_slots <= 0) pair_slots = sm_count / 2;
+  if (M == 0 || N == 0) {
+    pl->path = 0;
+    return HGEMM_OK;
+  }
+  if (K == 0 || !aligned16) {
+    pl->path = 2;
+    pl->tile_m = 64;
+    pl->tile_n = 64;
+    pl->pair = 1;
+    pl->tiles_m = ceil_div(M, 64);
+    pl->tiles_n = ceil_div(N, 64);
+    pl->grid_ctas = pl->tiles_m * pl->tiles_n;
+    return HGEMM_OK;
+  }
+  (void)beta;
+  pl->path = 1;
+  pl->lda = (K + 7) & ~7;
+  pl->ldb = (N + 7) & ~7;
+  pl->pad_a = pl->lda != K;
+  pl->pad_b = pl->ldb != N;
+  pl->scratch_bytes = ((pl->pad_a ? static_cast<size_t>(M) * pl->lda : 0) +
+                       (pl->pad_b ? static_cast<size_t>(K) * pl->ldb : 0)) *
+                      sizeof(__half);
+  pl->tma_store = (N % 8 == 0) ? 1 : 0;
+
+  int tile = tile_from_force(force_bm, force_bn);
+  if (tile < 0) {
+    // Preference order on ties: least operand traffic per flop first.
+    const int order[kNumTiles] = {kT256x256, kT256x128, kT128x256, kT128x128, kT128x64};
+    long long best = -1;
+    for (int o = 0; o < kNumTiles; ++o) {
+      const TileInfo &ti = kTiles[order[o]];
+      const long long tiles =
+          static_cast<long long>(ceil_div(M, CTA_M * ti.pair)) * ceil_div(N, ti.bn);
+      const long long slots = ti.pair == 2 ? pair_slots : sm_count;
+      const long long waves = (tiles + slots - 1) / slots;
+      // per-CTA critical path ~ waves x columns x (K + fixed per-tile overhead in k units)
+      const long long cost = waves * ti.bn * (static_cast<long long>(K) + 256);
+      if (best < 0 || cost < best) {
+        best = cost;
+        tile = order[o];
+      }
+    }
+  }
+  const TileInfo &ti = kTiles[tile];
+  pl->pair = ti.pair;
+  pl->tile_m = CTA_M * ti.pair;
+  pl->tile_n = ti.bn;
+  pl->stages = ti.stages;
+  pl->tiles_m = ceil_div(M, pl->tile_m);
+  pl->tiles_n = ceil_div(N, pl->tile_n);
+  const long long total = static_cast<long long>(pl->tiles_m) * pl->tiles_n;
+  const int slots = ti.pair == 2 ? pair_slots : sm_count;
+  const int units = static_cast<int>(std::min<long long>(total, slots));
+  pl->grid_ctas = units * ti.pair;
+  if (group_m == 0) {
+    // Working set of one wave ~ g tile-rows of A plus (units/g) tile-columns of B; choose g
+    // near sqrt(units * tile_n / tile_m) (equal A and B footprints), at least 1.
+    const double g = std::sqrt(static_cast<double>(units) * pl->tile_n / pl->tile_m);
+    group_m = std::max(1, static_cast<int>(g + 0.5));
+  }
+  pl->group_m = std::min(group_m, pl->tiles_m);
+  return HGEMM_OK;
+}
+
+// ---------------------------------------------------------------- scratch
+// Caller holds g_mu. Grow-only per-device buffer for restrided operands.
+void *scratch_get(DevState &d, size_t bytes) {
+  if (bytes <= d.scratch_bytes) return d.scratch;
+  if (d.scratch) {
+    cudaFree(d.scratch);
+    d.scratch = nullptr;
+    d.scratch_bytes = 0;
+  }
+  void *p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  d.scratch = p;
+  d.scratch_bytes = bytes;
+  return p;
+}
+
+int launch_restride(const __half *src, __half *dst, int rows, int cols, int ld, int sm_count,
+                    cudaStream_t stream) {
+  const long long groups = static_cast<long long>(rows) * (ld / 8);
+  const int blocks = static_cast<int>(std::min<long long>((groups + 255) / 256, sm_count * 8LL));
+  restride_kernel<<<std::max(blocks, 1), 256, 0, stream>>>(src, dst, rows, cols, ld);
+  return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
+}
+
+int launch_simt(const __half *A, const __half *B, __half *C, int M, int N, int K, float alpha,
+                float beta, cudaStream_t stream) {
+  dim3 grid(ceil_div(N, 64), ceil_div(M, 64));
+  hgemm_simt_kernel<<<grid, 256, 0, stream>>>(A, B, C, M, N, K, alpha, beta);
+  return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
+}
+
+// Launch the tcgen05 kernel for an already-made plan on operands with 16-byte strides.
+int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const __half *B,
+              int ldb, __half *C, int M, int N, int K, float alpha, float beta,
+              cudaStream_t stream, DevState &d) {
+  const TileInfo &ti = kTiles[tile];
+  const bool tma_epi = pl.tma_store != 0;
+  CUtensorMap ta, tb, tc;
+  if (!encode_2d(&ta, A, M, K, lda, CTA_M, BK) || !encode_2d(&tb, B, K, N, ldb, BK, 64))
+    return HGEMM_ERR_TENSOR_MAP;
+  if (tma_epi) {
+    if (!encode_2d(&tc, C, M, N, N, EPI_ROWS, EPI_COLS)) return HGEMM_ERR_TENSOR_MAP;
+  } else {
+    tc = ta;
+  }
+  KernelFn k = kernel_for(tile, tma_epi);
+  if (!d.attr_done[tile][tma_epi]) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, ti.smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return HGEMM_ERR_CUDA;
+    }
+    d.attr_done[tile][tma_epi] = true;
+  }
+  KParams kp;
+  kp.M = M;
+  kp.N = N;
+  kp.K = K;
+  kp.tiles_m = pl.tiles_m;
+  kp.tiles_n = pl.tiles_n;
+  kp.num_tiles = pl.tiles_m * pl.tiles_n;
+  kp.num_kb = ceil_div(K, BK);
+  kp.group_m = pl.group_m;
+  kp.alpha = alpha;
+  kp.beta = beta;
+  kp.C = C;
+  kp.timeout_ns = g_timeout_ns.load();
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid_ctas, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = ti.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ti.pair;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ti.pair == 2 ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, k, ta, tb, tc, kp) != cudaSuccess) {
+    cudaGetLastError();
+    return HGEMM_ERR_LAUNCH;
+  }
+  return HGEMM_OK;
+}
+
+int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K, float alpha,
+                float beta, cudaStream_t stream, int force_bm, int force_bn, int group_m) {
+  if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return HGEMM_OK;
+  if (!A || !B || !C) return HGEMM_ERR_INVALID_ARG;
+  int dev;
+  if (current_device(&dev) != HGEMM_OK) return HGEMM_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DevState *d = nullptr;
+  int st = ensure_device(dev, &d);
+  if (st != HGEMM_OK) return st;
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+  hgemm_plan_t pl;
+  st = make_plan(M, N, K, beta, aligned16, force_bm, force_bn, group_m, d->sm_count,
+                 d->pair_slots, &pl);
+  if (st != HGEMM_OK) return st;
+  if (pl.path == 0) return HGEMM_OK;
+  if (pl.path == 2) return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
+
+  const __half *Ause = A, *Buse = B;
+  if (pl.pad_a || pl.pad_b) {
+    __half *w = static_cast<__half *>(scratch_get(*d, pl.scratch_bytes));
+    if (!w) return HGEMM_ERR_ALLOC;
+    const size_t na = pl.pad_a ? static_cast<size_t>(M) * pl.lda : 0;
+    if (pl.pad_a) {
+      st = launch_restride(A, w, M, K, pl.lda, d->sm_count, stream);
+      if (st != HGEMM_OK) return st;
+      Ause = w;
+    }
+    if (pl.pad_b) {
+      st = launch_restride(B, w + na, K, N, pl.ldb, d->sm_count, stream);
+      if (st != HGEMM_OK) return st;
+      Buse = w + na;
+    }
+  }
+  int tile = -1;
+  for (int t = 0; t < kNumTiles; ++t)
+    if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;
+  return launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, C, M, N, K, alpha, beta, stream, *d);
+}
+
+// ---------------------------------------------------------------- autotune cache
+struct TuneCfg {
+  int bm, bn, group_m;
+};
+std::map<std::tuple<int, int, int, int>, TuneCfg> g_tune;
+
+}  // namespace
+}  // namespace hgemm
+
+// ============================================================================ C ABI
+using namespace hgemm;
+
+extern "C" {
+
+int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N,
+                    int K, float alpha, float beta, hgemm_stream_t stream, int force_bm,
+                    int force_bn, int group_m) {
+  return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
+                                reinterpret_cast<cudaStream_t>(stream), force_bm, force_bn,
+                                group_m));
+}
+
+int hgemm_launch(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N,
+                 int K, float alpha, float beta, hgemm_stream_t stream) {
+  return hgemm_launch_ex(A, B, C, M, N, K, alpha, beta, stream, 0, 0, 0);
+}
+
+void solve(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
+           float alpha, float beta) {
+  int st = launch_impl(A, B, C, M, N, K, alpha, beta, 0, 0, 0, 0);
+  const cudaError_t e = cudaDeviceSynchronize();
+  if (st == HGEMM_OK && e != cudaSuccess) st = HGEMM_ERR_CUDA;
+  if (st == HGEMM_OK) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_dev_status, sizeof(v)) == cudaSuccess && v != 0)
+      st = HGEMM_ERR_DEVICE_TIMEOUT;
+  }
+  set_status(st);
+}
+
+int hgemm_launch_tuned(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                       int N, int K, float alpha, float beta, hgemm_stream_t stream) {
+  int dev;
+  if (current_device(&dev) != HGEMM_OK) return set_status(HGEMM_ERR_CUDA);
+  const auto key = std::make_tuple(dev, M, N, K);
+  TuneCfg best{0, 0, 0};
+  bool have = false;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto it = g_tune.find(key);
+    if (it != g_tune.end()) {
+      best = it->second;
+      have = true;
+    }
+  }
+  const bool aligned = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+  if (!have && M > 0 && N > 0 && K > 0 && aligned) {
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    __half *scratchC = nullptr;
+    if (cudaMalloc(&scratchC, static_cast<size_t>(M) * N * sizeof(__half)) != cudaSuccess) {
+      cudaGetLastError();
+      return set_status(HGEMM_ERR_ALLOC);
+    }
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    const int bms[kNumTiles] = {256, 256, 128, 128, 128};
+    const int bns[kNumTiles] = {256, 128, 256, 128, 64};
+    const int gms[5] = {0, 4, 8, 16, 32};
+    float best_ms = 1e30f;
+    for (int t = 0; t < kNumTiles; ++t) {
+      for (int g : gms) {
+        bool ok = true;
+        for (int i = 0; i < 3 && ok; ++i)
+          ok = launch_impl(A, B, scratchC, M, N, K, alpha, 0.0f, s, bms[t], bns[t], g) == HGEMM_OK;
+        if (!ok || cudaStreamSynchronize(s) != cudaSuccess) continue;
+        cudaEventRecord(e0, s);
+        for (int i = 0; i < 5; ++i) launch_impl(A, B, scratchC, M, N, K, alpha, 0.0f, s, bms[t], bns[t], g);
+        cudaEventRecord(e1, s);
+        if (cudaEventSynchronize(e1) != cudaSuccess) continue;
+        float ms = 0;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (ms > 0 && ms < best_ms) {
+          best_ms = ms;
+          best = TuneCfg{bms[t], bns[t], g};
+        }
+      }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(scratchC);
+    cudaGetLastError();
+    std::lock_guard<std::mutex> lock(g_mu);
+    g_tune[key] = best;
+  }
+  return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
+                                reinterpret_cast<cudaStream_t>(stream), best.bm, best.bn,
+                                best.group_m));
+}
+
+int hgemm_last_status(void) { return t_last_status; }
+
+const char *hgemm_status_string(int s) {
+  switch (s) {
+    case HGEMM_OK: return "ok";
+    case HGEMM_ERR_INVALID_ARG: return "invalid argument";
+    case HGEMM_ERR_CUDA: return "CUDA runtime call failed";
+    case HGEMM_ERR_TENSOR_MAP: return "tensor map encode failed";
+    case HGEMM_ERR_ALLOC: return "scratch allocation failed";
+    case HGEMM_ERR_LAUNCH: return "kernel launch failed";
+    case HGEMM_ERR_DEVICE_TIMEOUT: return "bounded device wait ran out";
+    case HGEMM_ERR_UNSUPPORTED_DEVICE: return "device is not sm_100 (B200)";
+    case HGEMM_ERR_NCCL: return "NCCL unavailable or failed";
+    case HGEMM_ERR_TOO_LARGE: return "size beyond this entry point's limit";
+    default: return "unknown status";
+  }
+}
+
+int hgemm_device_status(int clear, int *where) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return set_status(HGEMM_ERR_CUDA);
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dev_status, sizeof(v)) != cudaSuccess)
+    return set_status(HGEMM_ERR_CUDA);
+  if (where) *where = static_cast<int>(v & 0xffu);
+  if (clear && v) {
+    const unsigned z = 0;
+    if (cudaMemcpyToSymbol(g_dev_status, &z, sizeof(z)) != cudaSuccess)
+      return set_status(HGEMM_ERR_CUDA);
+  }
+  return v ? HGEMM_ERR_DEVICE_TIMEOUT : HGEMM_OK;
+}
+
+void hgemm_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1ull); }
+
+int hgemm_selftest_wait_timeout(unsigned long long timeout_ns) {
+  int *d_out = nullptr;
+  if (cudaMalloc(&d_out, sizeof(int)) != cudaSuccess) return set_status(HGEMM_ERR_CUDA);
+  int h = -1;
+  wait_selftest_kernel<<<1, 32>>>(timeout_ns, d_out);
+  int st = (cudaGetLastError() == cudaSuccess) ? HGEMM_OK : HGEMM_ERR_LAUNCH;
+  if (st == HGEMM_OK && cudaMemcpy(&h, d_out, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    st = HGEMM_ERR_CUDA;
+  cudaFree(d_out);
+  int where = 0;
+  hgemm_device_status(1, &where);  // the self-test recorded a timeout: clear it
+  if (st != HGEMM_OK) return set_status(st);
+  set_status(HGEMM_OK);
+  return h;
+}
+
+void hgemm_release(void) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  for (int i = 0; i < 64; ++i) {
+    if (g_dev[i].scratch) {
+      cudaSetDevice(i);
+      cudaFree(g_dev[i].scratch);
+      g_dev[i].scratch = nullptr;
+      g_dev[i].scratch_bytes = 0;
+    }
+  }
+  cudaSetDevice(cur);
+  g_tune.clear();
+}
+
+int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int force_bn,
+               int group_m, int sm_count, int pair_slots, hgemm_plan_t *out) {
+  if (!out) return HGEMM_ERR_INVALID_ARG;
+  return make_plan(M, N, K, beta, aligned16 != 0, force_bm, force_bn, group_m, sm_count,
+                   pair_slots, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,145 @@
+/*
+ * hgemm_b200.h -- C ABI of the B200 (sm_100a) FP16 GEMM library `libhgemm_b200.so`.
+ *
+ *     C[M,N] = alpha * (A[M,K] @ B[K,N]) + beta * C[M,N]
+ *
+ * All matrices are row-major, IEEE binary16 in and out, fp32 accumulation; A, B and C are
+ * DEVICE pointers owned by the caller. C is both input (when beta != 0) and output, updated
+ * in place. When beta == 0, C is never read, so NaN/Inf already in C do not propagate.
+ * Each output element is alpha*acc (+ beta*C_in) computed in fp32 and rounded once to half
+ * with round-to-nearest-even.
+ *
+ * Every entry point takes plain pointers and sizes; nothing here depends on PyTorch.
+ * Reference interfaces replaced (yz-wqf/Hopper_GEMM):
+ *   solve              <- extern "C" solve(...)            mma_half.cu:1636-1640
+ *   hgemm_launch       <- h100_hgemm::launch(..., stream)  mma_half.cu:1530-1563
+ *   hgemm_launch_ex    <- h100_hgemm::launch(..., force_bm, force_bn, group_m)
+ *                                                         mma_half.cu:1530-1531
+ *   hgemm_launch_tuned <- h100_hgemm::launch_tuned(...)    mma_half.cu:1624-1628
+ *   hgemm_release      <- (the reference never frees g_pad, mma_half.cu:1308-1322)
+ */
+#ifndef HGEMM_B200_H_
+#define HGEMM_B200_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+#include <cuda_fp16.h>
+typedef __half hgemm_half_t;
+extern "C" {
+#else
+typedef unsigned short hgemm_half_t; /* IEEE binary16 bit pattern */
+#endif
+
+/* A CUDA stream handle (cudaStream_t / CUstream). 0 is the legacy default stream. */
+typedef struct CUstream_st *hgemm_stream_t;
+
+/* ---------------------------------------------------------------- status codes */
+#define HGEMM_OK 0
+#define HGEMM_ERR_INVALID_ARG 1      /* negative size, bad force_* tile, null pointer */
+#define HGEMM_ERR_CUDA 2             /* a CUDA runtime call failed (see hgemm_status_string) */
+#define HGEMM_ERR_TENSOR_MAP 3       /* cuTensorMapEncodeTiled rejected an operand */
+#define HGEMM_ERR_ALLOC 4            /* scratch allocation for a restrided operand failed */
+#define HGEMM_ERR_LAUNCH 5           /* kernel launch failed */
+#define HGEMM_ERR_DEVICE_TIMEOUT 6   /* a bounded wait inside a kernel ran out (device status) */
+#define HGEMM_ERR_UNSUPPORTED_DEVICE 7 /* not a compute capability 10.0 device */
+#define HGEMM_ERR_NCCL 8             /* NCCL missing or an NCCL call failed */
+#define HGEMM_ERR_TOO_LARGE 9        /* size beyond what this entry point supports */
+
+/* ---------------------------------------------------------------- GEMM entry points */
+
+/* Drop-in for the reference's `solve`: launches on the legacy default stream, then
+ * cudaDeviceSynchronize(). Returns nothing (like the reference); the outcome, including a
+ * device-side wait timeout observed after the synchronize, is kept for hgemm_last_status(). */
+void solve(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
+           float alpha, float beta);
+
+/* Asynchronous launch on `stream` with the automatic tile / raster choice.
+ * M == 0 or N == 0 is a no-op; K == 0 gives C = beta*C (alpha*0 added). Returns a status. */
+int hgemm_launch(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N,
+                 int K, float alpha, float beta, hgemm_stream_t stream);
+
+/* Same, with the reference's override knobs. force_bm in {0, 128, 256} (256 = a 2-SM
+ * UMMA pair of two 128-row CTAs), force_bn in {0, 64, 128, 256}; 0 means automatic.
+ * Valid explicit tiles: 256x256, 256x128, 128x256, 128x128, 128x64. group_m = raster band
+ * height in tile rows (0 = automatic). */
+int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N,
+                    int K, float alpha, float beta, hgemm_stream_t stream, int force_bm,
+                    int force_bn, int group_m);
+
+/* Opt-in autotuned launch: the first call per (device, M, N, K) times every tile x group_m
+ * candidate (into a temporary output, so C is not disturbed) and caches the winner. */
+int hgemm_launch_tuned(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                       int N, int K, float alpha, float beta, hgemm_stream_t stream);
+
+/* ---------------------------------------------------------------- status, planning */
+
+/* Status of the last call made by this host thread. */
+int hgemm_last_status(void);
+const char *hgemm_status_string(int status);
+
+/* Device-side status word of the current device: HGEMM_OK, or HGEMM_ERR_DEVICE_TIMEOUT
+ * when some kernel's bounded wait ran out since the last clear. Synchronizes the device.
+ * `where` (may be NULL) receives the code of the wait that gave up. */
+int hgemm_device_status(int clear, int *where);
+
+/* Upper bound, in nanoseconds, on any single wait inside the GEMM kernels (default 2e9). */
+void hgemm_set_wait_timeout_ns(unsigned long long ns);
+
+/* Launches a kernel whose only wait is on an mbarrier that nothing arrives on, bounded by
+ * `timeout_ns`, and returns the status that kernel reported (HGEMM_ERR_DEVICE_TIMEOUT when
+ * the bound works). Leaves the CUDA context usable; clears the device status word. */
+int hgemm_selftest_wait_timeout(unsigned long long timeout_ns);
+
+/* Frees the per-device scratch used to restride A (K % 8 != 0) or B (N % 8 != 0). */
+void hgemm_release(void);
+
+/* Host-only description of what hgemm_launch_ex would run; needs no GPU. */
+typedef struct {
+  int path;       /* 0 no-op, 1 tcgen05 tiles, 2 SIMT fallback */
+  int tile_m;     /* rows per tile: 128 (one CTA) or 256 (2-SM pair) */
+  int tile_n;     /* columns per tile */
+  int pair;       /* 1 or 2 CTAs per UMMA */
+  int group_m;    /* raster band height in tile rows */
+  int stages;     /* smem pipeline depth */
+  int tiles_m, tiles_n;
+  int grid_ctas;  /* persistent CTAs launched */
+  int pad_a, pad_b;      /* operand restrided into scratch (K % 8, N % 8) */
+  int lda, ldb;          /* leading dimensions the tensor maps use */
+  int tma_store;         /* 1: TMA-store epilogue (N % 8 == 0), 0: SIMT stores */
+  size_t scratch_bytes;  /* scratch needed for restrided operands */
+} hgemm_plan_t;
+
+/* `aligned16` says whether A, B and C all start on 16-byte boundaries; `sm_count` and
+ * `pair_slots` (co-resident 2-CTA clusters) describe the device (<= 0: B200 defaults). */
+int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int force_bn,
+               int group_m, int sm_count, int pair_slots, hgemm_plan_t *out);
+
+/* ---------------------------------------------------------------- multi-GPU (row shards)
+ * One process per GPU. Rank r owns rows [row_begin(r), row_begin(r+1)) of A and C, with
+ * row_begin(r) = (M * r) / nranks; B is replicated. hgemm_sharded_rank computes the local
+ * C row block with the GEMM above and all-gathers C in place over NCCL, so every rank ends
+ * with the full C. The reference is single-GPU; this layer has no counterpart there.
+ * NCCL is loaded at run time (libnccl.so.2); without it these return HGEMM_ERR_NCCL. */
+typedef struct hgemm_comm_s *hgemm_comm_t;
+
+int hgemm_comm_unique_id(void *id_out, size_t id_bytes); /* id_bytes >= 128 */
+int hgemm_comm_init(hgemm_comm_t *comm, int nranks, const void *id, size_t id_bytes, int rank);
+int hgemm_comm_destroy(hgemm_comm_t comm);
+
+/* A_local: this rank's rows of A (rows x K); B: full K x N on this device; C: full M x N on
+ * this device (the local row block is read when beta != 0). Equal row blocks
+ * (M % nranks == 0) gather in place with one ncclAllGather; otherwise per-rank broadcasts.
+ * `chunks` > 1 splits the local rows so the gather of chunk c overlaps the GEMM of c+1. */
+int hgemm_sharded_rank(hgemm_comm_t comm, const hgemm_half_t *A_local, const hgemm_half_t *B,
+                       hgemm_half_t *C, int M, int N, int K, float alpha, float beta,
+                       int chunks, hgemm_stream_t stream);
+
+/* Row range helper, identical to the one hgemm_sharded_rank uses. */
+int hgemm_shard_rows(int M, int nranks, int rank, int *row_begin, int *row_count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HGEMM_B200_H_ */

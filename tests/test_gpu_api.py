@@ -1,0 +1,114 @@
+"""GPU: semantics of the drop-in entry points (mma_half.cu:1530-1640 behaviour) and the
+bounded-wait failure path."""
+import numpy as np
+import pytest
+import torch
+
+from tests.gpu_util import dev, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(oracle, M, N, K, seed=1):
+    g = oracle.MT19937Stream(seed)
+    return g.uniform_half((M, K)), g.uniform_half((K, N)), g.uniform_half((M, N))
+
+
+def test_beta_zero_never_reads_c(cuda, oracle):
+    A, B, _ = _inputs(oracle, 200, 136, 72)
+    for N in (136, 135):  # TMA-store epilogue and the SIMT epilogue
+        Bn = np.ascontiguousarray(B[:, :N])
+        dA, dB = dev(A), dev(Bn)
+        dC = torch.full((200, N), float("nan"), dtype=torch.float16, device="cuda")
+        cuda.solve(dA, dB, dC, 200, N, 72, 1.0, 0.0)
+        out = host(dC)
+        assert np.isfinite(out).all()
+        ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, Bn), 72)
+        assert ok, worst
+
+
+def test_k_zero_scales_c(cuda, oracle):
+    _, _, C = _inputs(oracle, 64, 48, 8)
+    dC = dev(C)
+    dummy = torch.zeros(16, dtype=torch.float16, device="cuda")
+    cuda.solve(dummy, dummy, dC, 64, 48, 0, 2.0, -0.5)
+    assert cuda.last_status() == 0
+    want = oracle.f32_to_f16((-0.5 * C.astype(np.float32)).astype(np.float32))
+    assert np.array_equal(host(dC).view(np.uint16), want.view(np.uint16))
+
+
+def test_empty_m_or_n_is_noop(cuda):
+    C = torch.full((4, 4), 3.0, dtype=torch.float16, device="cuda")
+    a = torch.zeros(16, dtype=torch.float16, device="cuda")
+    cuda.solve(a, a, C, 0, 4, 4, 1.0, 0.0)
+    cuda.solve(a, a, C, 4, 0, 4, 1.0, 0.0)
+    assert cuda.last_status() == 0
+    assert bool((C == 3.0).all())
+
+
+def test_misaligned_pointers_fall_back(cuda, oracle):
+    M, N, K = 70, 90, 50
+    A, B, C = _inputs(oracle, M, N, K, seed=4)
+    bufA = torch.zeros(M * K + 1, dtype=torch.float16, device="cuda")
+    bufB = torch.zeros(K * N + 1, dtype=torch.float16, device="cuda")
+    bufC = torch.zeros(M * N + 1, dtype=torch.float16, device="cuda")
+    bufA[1:] = dev(A).view(-1)
+    bufB[1:] = dev(B).view(-1)
+    bufC[1:] = dev(C).view(-1)
+    esz = 2
+    cuda.solve(bufA.data_ptr() + esz, bufB.data_ptr() + esz, bufC.data_ptr() + esz, M, N, K,
+               1.25, 0.75)
+    assert cuda.last_status() == 0
+    out = host(bufC)[1:].reshape(M, N)
+    ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B, C, 1.25, 0.75), K)
+    assert ok, worst
+
+
+def test_side_stream_launch(cuda, oracle):
+    M, N, K = 512, 512, 512
+    A, B, _ = _inputs(oracle, M, N, K, seed=5)
+    dA, dB = dev(A), dev(B)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        dC = cuda.gemm(dA, dB, stream=s)
+    s.synchronize()
+    ok, worst, _ = oracle.check(host(dC), oracle.gemm_f64(A, B), K)
+    assert ok, worst
+
+
+def test_deterministic_bits(cuda, oracle):
+    A, B, _ = _inputs(oracle, 1536, 1280, 2000, seed=6)
+    dA, dB = dev(A), dev(B)
+    r1 = host(cuda.gemm(dA, dB))
+    r2 = host(cuda.gemm(dA, dB))
+    assert np.array_equal(r1.view(np.uint16), r2.view(np.uint16))
+
+
+def test_tuned_launch_matches_default(cuda, oracle):
+    M, N, K = 768, 640, 384
+    A, B, C = _inputs(oracle, M, N, K, seed=8)
+    dA, dB = dev(A), dev(B)
+    dC = dev(C)
+    cuda.launch_tuned(dA, dB, dC, M, N, K, 1.0, 0.5)
+    torch.cuda.synchronize()
+    ok, worst, _ = oracle.check(host(dC), oracle.gemm_f64(A, B, C, 1.0, 0.5), K)
+    assert ok, worst  # C was not clobbered by the search (beta != 0 still correct)
+    dC2 = dev(C)
+    cuda.launch_tuned(dA, dB, dC2, M, N, K, 1.0, 0.5)  # cached plan
+    assert np.array_equal(host(dC).view(np.uint16), host(dC2).view(np.uint16))
+
+
+def test_bounded_wait_gives_up_and_context_survives(cuda, oracle):
+    """A kernel waiting on an mbarrier nothing arrives on must return an error status after
+    its bound, with the context still usable."""
+    st = cuda.selftest_wait_timeout(20_000_000)  # 20 ms
+    assert st == cuda.HGEMM_ERR_DEVICE_TIMEOUT
+    assert cuda.device_status(clear=True)[0] == 0
+    A, B, _ = _inputs(oracle, 256, 256, 256, seed=9)
+    out = host(cuda.gemm(dev(A), dev(B)))
+    ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B), 256)
+    assert ok, worst
+
+
+def test_device_status_clean(cuda):
+    assert cuda.device_status(clear=False)[0] == 0

@@ -1,0 +1,70 @@
+"""CPU: the per-shape dispatcher (the B200 counterpart of launch_mainloop / launch,
+mma_half.cu:1441-1563), exercised through the host-only hgemm_plan()."""
+import pytest
+
+import hopper_gemm_b200 as hg
+
+B200 = dict(sm_count=148, pair_slots=74)
+
+
+def test_noop_and_fallback_paths():
+    assert hg.plan(0, 128, 64, **B200)["path"] == 0
+    assert hg.plan(128, 0, 64, **B200)["path"] == 0
+    # K == 0 and misaligned pointers take the SIMT path (the reference's gemm_fallback route)
+    assert hg.plan(128, 128, 0, **B200)["path"] == 2
+    assert hg.plan(128, 128, 64, aligned16=False, **B200)["path"] == 2
+
+
+@pytest.mark.parametrize("M,N,K,pad_a,pad_b,tma", [
+    (4095, 4095, 4095, 1, 1, 0),     # both operands restrided, SIMT stores (N odd)
+    (4096, 4095, 4096, 0, 1, 0),
+    (2048, 2047, 2048, 0, 1, 0),
+    (3000, 1000, 2000, 0, 0, 1),     # aligned strides, ragged tiles only
+    (1023, 1, 1025, 1, 1, 0),
+    (8192, 8192, 8192, 0, 0, 1),
+])
+def test_restride_and_epilogue_choice(M, N, K, pad_a, pad_b, tma):
+    p = hg.plan(M, N, K, **B200)
+    assert p["path"] == 1
+    assert (p["pad_a"], p["pad_b"], p["tma_store"]) == (pad_a, pad_b, tma)
+    assert p["lda"] % 8 == 0 and p["ldb"] % 8 == 0
+    assert p["lda"] >= K and p["ldb"] >= N
+    want = 2 * ((M * p["lda"] if pad_a else 0) + (K * p["ldb"] if pad_b else 0))
+    assert p["scratch_bytes"] == want
+
+
+def test_large_square_uses_pair_tile():
+    p = hg.plan(8192, 8192, 8192, **B200)
+    assert (p["tile_m"], p["tile_n"], p["pair"]) == (256, 256, 2)
+    assert p["grid_ctas"] == 148 and p["stages"] >= 4
+    assert 1 <= p["group_m"] <= p["tiles_m"]
+
+
+def test_small_problem_spreads_over_sms():
+    p = hg.plan(1024, 1024, 1024, **B200)
+    tiles = p["tiles_m"] * p["tiles_n"]
+    assert tiles * p["pair"] >= 64  # uses at least 64 SMs
+    assert p["grid_ctas"] <= 148
+
+
+@pytest.mark.parametrize("bm,bn", [(256, 256), (256, 128), (128, 256), (128, 128), (128, 64)])
+def test_forced_tiles(bm, bn):
+    p = hg.plan(2048, 2048, 512, force_bm=bm, force_bn=bn, **B200)
+    assert (p["tile_m"], p["tile_n"]) == (bm, bn)
+    assert p["pair"] == bm // 128
+    assert p["grid_ctas"] % p["pair"] == 0
+
+
+def test_invalid_forced_tile_rejected():
+    with pytest.raises(hg.HgemmError):
+        hg.plan(256, 256, 256, force_bm=64, force_bn=64, **B200)
+    with pytest.raises(hg.HgemmError):
+        hg.plan(256, 256, 256, force_bm=256, force_bn=64, **B200)
+
+
+def test_grid_never_exceeds_resident_slots():
+    for M, N, K in [(16384, 16384, 16384), (384, 2048, 2048), (1, 4096, 4096), (8192, 8, 8192)]:
+        p = hg.plan(M, N, K, **B200)
+        slots = 74 if p["pair"] == 2 else 148
+        assert p["grid_ctas"] // p["pair"] <= slots
+        assert p["grid_ctas"] // p["pair"] <= p["tiles_m"] * p["tiles_n"]
