@@ -36,13 +36,16 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--M", type=int, default=8192, help="rows per GPU")
     ap.add_argument("--N", type=int, default=8192)
     ap.add_argument("--K", type=int, default=8192)
     ap.add_argument("--chunks", type=int, default=1, help="row chunks for gather overlap (N>1)")
+    ap.add_argument("--force-bm", type=int, default=0, help="tile rows (0 = automatic)")
+    ap.add_argument("--force-bn", type=int, default=0, help="tile columns (0 = automatic)")
+    ap.add_argument("--group-m", type=int, default=0, help="raster band height (0 = automatic)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -72,62 +75,78 @@ def profiled_traffic(M, N, K):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """SM clock, power and throttle reasons sampled through NVML every 10 ms while the timed
+    region runs (falls back to `nvidia-smi -lms 100` when pynvml is missing)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
-        self.lines = []
+        self.samples = []  # (sm_mhz, max_mhz, power_w, reasons_bitmask)
+        self.stop = threading.Event()
+        self.thread = None
+
+    def _poll_nvml(self):
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), mx,
+                                     pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                     pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except pynvml.NVMLError:
+                pass
+            self.stop.wait(0.01)
+
+    def _poll_smi(self):
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        bits = [0x8, 0x40, 0x20, 0x4]
+        proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={fields}",
+                                 "--format=csv,noheader,nounits", "-lms", "100"],
+                                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        try:
+            for line in proc.stdout:
+                if self.stop.is_set():
+                    break
+                p = [x.strip() for x in line.split(",")]
+                try:
+                    mask = sum(b for b, v in zip(bits, p[3:7]) if v.lower() == "active")
+                    self.samples.append((float(p[0]), float(p[1]), float(p[2]), mask))
+                except (ValueError, IndexError):
+                    continue
+        finally:
+            proc.terminate()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml  # noqa: F401
+            target = self._poll_nvml
+        except ImportError:
+            target = self._poll_smi
+        self.thread = threading.Thread(target=target, daemon=True)
+        self.thread.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.thread.join(timeout=2)
+        self.stop.set()
+        self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx = [], None
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[4:8]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        if not sm:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        mask = 0
+        for s in self.samples:
+            mask |= int(s[3])
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": self.samples[0][1],
+                "power_w_median": statistics.median(s[2] for s in self.samples),
+                "reasons": sorted(k for k, b in self.REASONS.items() if mask & b),
+                "samples": len(self.samples)}
 
 
 def hash_fill_(t, seed):
@@ -187,7 +206,7 @@ def run_reference(args, rank, world):
     M, N, K = args.M * world, args.N, args.K
     threads = orc.max_threads()
     B = orc.hash_fill_half((K, N), 0x85EBCA6B)
-    rows = max(threads, 2 * threads)
+    rows = 8 * threads
     A = orc.hash_fill_half((rows, K), 0x9E3779B9)
     for _ in range(max(args.warmup, 0)):
         orc.gemm_f64(A, B, rows=np.arange(threads), threads=threads)
@@ -267,8 +286,8 @@ def main():
 
     def ours():
         if comm is None:
-            st = hg.lib.hgemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), Ml, N, K, 1.0,
-                                     0.0, sptr)
+            st = hg.lib.hgemm_launch_ex(A.data_ptr(), B.data_ptr(), C.data_ptr(), Ml, N, K, 1.0,
+                                        0.0, sptr, args.force_bm, args.force_bn, args.group_m)
         else:
             st = hg.lib.hgemm_sharded_rank(comm, A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N,
                                            K, 1.0, 0.0, args.chunks, sptr)

@@ -56,7 +56,7 @@ constexpr int EPI_ROWS = 32;    // rows per epilogue warp (its TMEM lane quarter
 constexpr int EPI_COLS = 64;    // columns per epilogue chunk (one 128-byte swizzle row)
 constexpr int NUM_THREADS = 192;
 constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in dynamic shared memory per block
-constexpr int BAR_BYTES = 256;
+constexpr int BAR_BYTES = 512;
 
 // Device status word: 0, or kDevTimeout | where. Written once per failure (first wins).
 constexpr unsigned kDevTimeout = 0x100u;
@@ -67,29 +67,37 @@ enum WaitSite : unsigned {
   kSiteEpiTmemFull = 4,
   kSiteDrain = 5,
   kSiteSelftest = 6,
+  kSiteSchedEmpty = 7,
+  kSiteSchedFull = 8,
+  kSiteClc = 9,
 };
 __device__ unsigned int g_dev_status = 0;
 
 template <int PAIR, int BN>
 struct TileCfg {
-  static constexpr int B_COLS = BN / PAIR;  // B columns this CTA loads
-  static constexpr int B_BOXES = B_COLS / 64;
-  static constexpr int A_BYTES = CTA_M * BK * 2;  // 16 KB
+  static constexpr int UMMA_N = BN < 256 ? BN : 256;        // N of one tcgen05.mma
+  static constexpr int N_SUB = BN / UMMA_N;                  // UMMAs per k16 step
+  static constexpr int ACC_BUFS = (2 * BN <= 512) ? 2 : 1;   // TMEM accumulator buffers
+  static constexpr int SUB_COLS = UMMA_N / PAIR;             // B columns per CTA per UMMA
+  static constexpr int SUB_BOXES = SUB_COLS / 64;            // 64-column TMA boxes each
+  static constexpr int B_COLS = BN / PAIR;                   // B columns this CTA loads
+  static constexpr int A_BYTES = CTA_M * BK * 2;             // 16 KB
   static constexpr int B_BYTES = B_COLS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TX_BYTES = STAGE_BYTES * PAIR;  // armed on the leader's barrier
-  static constexpr int EPI_BYTES = 4 * 2 * EPI_ROWS * 128;  // 4 warps x 2 buffers x 4 KB
+  static constexpr int TX_BYTES = STAGE_BYTES * PAIR;        // armed on the leader's barrier
+  static constexpr int EPI_BYTES = 4 * 2 * EPI_ROWS * 128;   // 4 warps x 2 buffers x 4 KB
   static constexpr int STAGES_FIT = (SMEM_LIMIT - EPI_BYTES - 1024 - BAR_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;  // two accumulator buffers
+  static constexpr int TMEM_COLS = BN * ACC_BUFS;
   static constexpr int UMMA_M = CTA_M * PAIR;
-  static_assert(B_COLS % 64 == 0, "B slice must be whole 64-column swizzle blocks");
+  static constexpr int SCHED_SLOTS = 4;                      // tile-index ring depth
+  static_assert(SUB_COLS % 64 == 0, "B slice must be whole 64-column swizzle blocks");
   static_assert(STAGES >= 3, "pipeline too shallow");
   static_assert(SMEM <= SMEM_LIMIT, "shared memory over budget");
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0,
                 "TMEM allocation must be a power of two in [32, 512]");
-  static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
+  static_assert(UMMA_N % 16 == 0 && UMMA_N <= 256, "UMMA N");
 };
 
 struct KParams {
@@ -160,6 +168,13 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int j) {
 }
 
 // ============================================================================ the kernel
+// Work distribution: the grid has one cluster (PAIR CTAs) per output tile. Each running
+// cluster starts on its own tile and then takes over tiles of clusters that have not started
+// yet through cluster launch control (clusterlaunchcontrol.try_cancel), so the tiles spread
+// over the SMs by how fast each one actually goes (the two dies and their GPCs do not run at
+// one clock under the power cap). The leader CTA's producer thread owns that sequence and
+// publishes every tile index through a small shared-memory ring that the other roles of
+// both CTAs read; -1 ends the sequence.
 template <int PAIR, int BN, bool TMA_EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     hgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -167,6 +182,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
   using Cfg = TileCfg<PAIR, BN>;
   constexpr int S = Cfg::STAGES;
+  constexpr int NSL = Cfg::SCHED_SLOTS;
+  constexpr int ACC_BUFS = Cfg::ACC_BUFS;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
@@ -176,19 +193,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t sB0 = base + S * Cfg::A_BYTES;
   uint8_t *epi = smem + S * Cfg::STAGE_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(epi + Cfg::EPI_BYTES);
-  uint64_t *full = bars;             // [S]   TMA bytes landed (leader CTA's copy is used)
-  uint64_t *empty = bars + S;        // [S]   UMMA finished reading the stage
-  uint64_t *tfull = bars + 2 * S;    // [2]   accumulator buffer ready for the epilogue
-  uint64_t *tempty = bars + 2 * S + 2;  // [2] epilogue drained the accumulator buffer
-  uint64_t *drain = bars + 2 * S + 4;   // [1] teardown: all issued UMMAs retired
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  uint64_t *full = bars;                    // [S]   TMA bytes landed (leader CTA's copy is used)
+  uint64_t *empty = bars + S;               // [S]   UMMA finished reading the stage
+  uint64_t *tfull = bars + 2 * S;           // [2]   accumulator buffer ready for the epilogue
+  uint64_t *tempty = bars + 2 * S + 2;      // [2]   epilogue drained the accumulator buffer
+  uint64_t *drain = bars + 2 * S + 4;       // [1]   teardown: all issued UMMAs retired
+  uint64_t *sched_full = bars + 2 * S + 5;  // [NSL] tile index written
+  uint64_t *sched_empty = bars + 2 * S + 5 + NSL;  // [NSL] every reader took it (leader's copy)
+  uint64_t *clc_bar = bars + 2 * S + 5 + 2 * NSL;  // [1]  launch-control response landed
+  uint8_t *misc = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(bars + 2 * S + 6 + 2 * NSL) + 15) & ~uintptr_t(15));
+  uint8_t *clc_resp = misc;                                      // 16 bytes
+  volatile int *sched_val = reinterpret_cast<volatile int *>(misc + 16);  // [NSL]
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(misc + 16 + 4 * NSL);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(misc + 20 + 4 * NSL);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = (PAIR == 2) ? ptx::cluster_ctarank() : 0u;
-  const int cid = (PAIR == 2) ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
-  const int ncl = (PAIR == 2) ? static_cast<int>(ptx::nclusters_x()) : static_cast<int>(gridDim.x);
+  const int first_tile = (PAIR == 2) ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -200,6 +223,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::mbar_init(ptx::smem_u32(&tempty[a]), 4 * PAIR);
     }
     ptx::mbar_init(ptx::smem_u32(drain), 1);
+    // Readers of each tile index: leader MMA + 4 epilogue warps (+ the peer's producer and
+    // 4 epilogue warps for a pair).
+    for (int i = 0; i < NSL; ++i) {
+      ptx::mbar_init(ptx::smem_u32(&sched_full[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sched_empty[i]), PAIR == 2 ? 10 : 5);
+    }
+    ptx::mbar_init(ptx::smem_u32(clc_bar), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
   }
@@ -220,8 +250,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   WaitCtx wctx;
   wctx.abort_flag = abort_flag;
-  wctx.peer_abort = (PAIR == 2) ? ptx::mapa(ptx::smem_u32(const_cast<int *>(abort_flag)), rank ^ 1u) : 0u;
+  wctx.peer_abort =
+      (PAIR == 2) ? ptx::mapa(ptx::smem_u32(const_cast<int *>(abort_flag)), rank ^ 1u) : 0u;
   wctx.timeout_ns = p.timeout_ns;
+
+  // Readers take tile indices in ring order and release each slot to the leader's producer.
+  const uint32_t sched_empty_leader0 =
+      (PAIR == 2) ? ptx::mapa(ptx::smem_u32(&sched_empty[0]), 0u) : ptx::smem_u32(&sched_empty[0]);
+  auto sched_read = [&](int &slot, uint32_t &sph, int &tile) -> bool {
+    if (!wait_bar<PAIR == 2>(ptx::smem_u32(&sched_full[slot]), sph, wctx, kSiteSchedFull))
+      return false;
+    tile = sched_val[slot];
+    const uint32_t eb = sched_empty_leader0 + static_cast<uint32_t>(slot) * 8u;
+    if (PAIR == 2)
+      ptx::mbar_arrive_cluster(eb);
+    else
+      ptx::mbar_arrive(eb);
+    if (++slot == NSL) {
+      slot = 0;
+      sph ^= 1u;
+    }
+    return true;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -229,39 +279,123 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       long long issued = 0;
+      bool ok = true;
+      int sslot = 0;
+      uint32_t sph = 0;
       const uint32_t full_leader0 =
           (PAIR == 2) ? ptx::mapa(ptx::smem_u32(&full[0]), 0u) : ptx::smem_u32(&full[0]);
-      bool ok = true;
-      for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+
+      // All k-blocks of one tile: this CTA's 128 rows of A and its share of B's columns
+      // (for UMMA j, columns [j*UMMA_N + rank*SUB_COLS, +SUB_COLS) of the tile).
+      auto load_tile = [&](int tile) -> bool {
         int tm, tn;
-        decode_tile(t, p, tm, tn);
+        decode_tile(tile, p, tm, tn);
         const int arow = tm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M;
-        const int bcol = tn * BN + static_cast<int>(rank) * Cfg::B_COLS;
+        const int bcol = tn * BN + static_cast<int>(rank) * Cfg::SUB_COLS;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!wait_bar<false>(ptx::smem_u32(&empty[s]), ph ^ 1u, wctx, kSiteProducerEmpty)) {
-            ok = false;
-            break;
-          }
+          if (!wait_bar<false>(ptx::smem_u32(&empty[s]), ph ^ 1u, wctx, kSiteProducerEmpty))
+            return false;
           const uint32_t fbar = full_leader0 + static_cast<uint32_t>(s) * 8u;
           if (rank == 0) ptx::mbar_arrive_expect_tx(ptx::smem_u32(&full[s]), Cfg::TX_BYTES);
           const uint32_t dA = sA0 + static_cast<uint32_t>(s) * Cfg::A_BYTES;
           const uint32_t dB = sB0 + static_cast<uint32_t>(s) * Cfg::B_BYTES;
-          if (PAIR == 2) {
+          if (PAIR == 2)
             ptx::tma_load_2d_pair(&tmA, dA, fbar, kb * BK, arow);
-#pragma unroll
-            for (int b = 0; b < Cfg::B_BOXES; ++b)
-              ptx::tma_load_2d_pair(&tmB, dB + b * (BK * 128), fbar, bcol + 64 * b, kb * BK);
-          } else {
+          else
             ptx::tma_load_2d(&tmA, dA, fbar, kb * BK, arow);
 #pragma unroll
-            for (int b = 0; b < Cfg::B_BOXES; ++b)
-              ptx::tma_load_2d(&tmB, dB + b * (BK * 128), fbar, bcol + 64 * b, kb * BK);
+          for (int j = 0; j < Cfg::N_SUB; ++j) {
+#pragma unroll
+            for (int b = 0; b < Cfg::SUB_BOXES; ++b) {
+              const uint32_t dst = dB + static_cast<uint32_t>(j * Cfg::SUB_BOXES + b) * (BK * 128);
+              const int col = bcol + j * Cfg::UMMA_N + 64 * b;
+              if (PAIR == 2)
+                ptx::tma_load_2d_pair(&tmB, dst, fbar, col, kb * BK);
+              else
+                ptx::tma_load_2d(&tmB, dst, fbar, col, kb * BK);
+            }
           }
           ++issued;
           if (++s == S) {
             s = 0;
             ph ^= 1u;
           }
+        }
+        return true;
+      };
+
+      if (rank == 0) {
+        // Scheduler: publish each tile index to the ring (both CTAs' copies of the slot).
+        auto publish = [&](int v) -> bool {
+          if (!wait_bar<PAIR == 2>(ptx::smem_u32(&sched_empty[sslot]), sph ^ 1u, wctx,
+                                   kSiteSchedEmpty))
+            return false;
+          sched_val[sslot] = v;
+          const uint32_t fb = ptx::smem_u32(&sched_full[sslot]);
+          if (PAIR == 2) {
+            ptx::st_cluster_u32(ptx::mapa(ptx::smem_u32(const_cast<int *>(&sched_val[sslot])), 1u),
+                                static_cast<uint32_t>(v));
+            ptx::mbar_arrive_cluster(ptx::mapa(fb, 1u));
+          }
+          ptx::mbar_arrive(fb);
+          if (++sslot == NSL) {
+            sslot = 0;
+            sph ^= 1u;
+          }
+          return true;
+        };
+        bool clc_live = true, clc_pending = false;
+        uint32_t clc_ph = 0;
+        int tile = first_tile;
+        ok = publish(tile);
+        while (ok && tile >= 0) {
+          if (clc_live) {
+            // Ask for the next tile now; the answer is needed only after this tile's loads.
+            ptx::mbar_arrive_expect_tx(ptx::smem_u32(clc_bar), 16);
+            ptx::clc_try_cancel(ptx::smem_u32(clc_resp), ptx::smem_u32(clc_bar));
+            clc_pending = true;
+          }
+          if (!load_tile(tile)) {
+            ok = false;
+            break;
+          }
+          int next = -1;
+          if (clc_live) {
+            if (!wait_bar<false>(ptx::smem_u32(clc_bar), clc_ph, wctx, kSiteClc)) {
+              ok = false;
+              break;
+            }
+            clc_pending = false;
+            clc_ph ^= 1u;
+            uint32_t x = 0;
+            if (ptx::clc_query(ptx::smem_u32(clc_resp), x))
+              next = static_cast<int>(x) / PAIR;
+            else
+              clc_live = false;  // nothing left to take; never ask again
+            ptx::fence_proxy_async_smem();
+          }
+          ok = publish(next);
+          tile = next;
+        }
+        if (!ok && clc_pending) {
+          // Unwinding: the launch-control response must land before the CTA exits.
+          WaitCtx dctx = wctx;
+          volatile int no_abort = 0;
+          dctx.abort_flag = &no_abort;
+          dctx.peer_abort = 0;
+          dctx.timeout_ns = 50000000ull;
+          wait_bar<false>(ptx::smem_u32(clc_bar), clc_ph, dctx, kSiteDrain);
+        }
+      } else {
+        // The pair's second CTA follows the leader's tile sequence.
+        int tile = -1;
+        while (ok) {
+          if (!sched_read(sslot, sph, tile)) {
+            ok = false;
+            break;
+          }
+          if (tile < 0) break;
+          ok = load_tile(tile);
         }
       }
       if (!ok && rank == 0) {
@@ -281,46 +415,131 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ UMMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = ptx::umma_idesc_f16_f32(Cfg::UMMA_M, BN);
+      constexpr uint32_t idesc = ptx::umma_idesc_f16_f32(Cfg::UMMA_M, Cfg::UMMA_N);
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
+      int sslot = 0;
+      uint32_t sph = 0;
       bool issued_any = false;
       bool ok = true;
-      for (int t = cid; t < p.num_tiles && ok; t += ncl, ++it) {
-        const int acc = it & 1;
-        const uint32_t aph = static_cast<uint32_t>(it >> 1) & 1u;
-        if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[acc]), aph ^ 1u, wctx, kSiteMmaTmemEmpty)) {
+      uint32_t dtm = tmem_base;
+      // UMMA j (N-slice j) of one pipeline stage; A (K-major) advances 32 bytes per k16
+      // inside the swizzle row, B (N-major) 16 rows of 128 bytes per k16, and UMMA j reads
+      // the next SUB_BOXES blocks of 8 KB. Descriptor start addresses are in 16-byte units.
+      auto issue_sub = [&](int stage, int kb, int j) {
+        const uint64_t adesc = ptx::umma_desc_sw128(sA0 + stage * Cfg::A_BYTES, 16, 1024);
+        const uint64_t bdesc = ptx::umma_desc_sw128(sB0 + stage * Cfg::B_BYTES, BK * 128, 1024);
+#pragma unroll
+        for (int k = 0; k < BK / UMMA_K; ++k)
+          ptx::umma_f16<PAIR>(dtm + static_cast<uint32_t>(j * Cfg::UMMA_N),
+                              adesc + static_cast<uint64_t>(2 * k),
+                              bdesc + static_cast<uint64_t>(128 * k + j * Cfg::SUB_BOXES * (BK * 128 / 16)),
+                              idesc, (kb | k) != 0 ? 1u : 0u);
+        issued_any = true;
+      };
+      auto release_stage = [&](int stage) {
+        const uint32_t eb = ptx::smem_u32(&empty[stage]);
+        if (PAIR == 2)
+          ptx::umma_commit_pair_mask(eb, 0x3);  // both CTAs' copies of empty[stage]
+        else
+          ptx::umma_commit<1>(eb);
+      };
+      while (ok) {
+        int tile = -1;
+        if (!sched_read(sslot, sph, tile)) {
           ok = false;
           break;
         }
-        ptx::tc_fence_after();
-        const uint32_t dtm = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) {
+        if (tile < 0) break;
+        const int acc = it % ACC_BUFS;
+        const uint32_t aph = static_cast<uint32_t>(it / ACC_BUFS) & 1u;
+        if constexpr (ACC_BUFS == 2) {
+          if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[acc]), aph ^ 1u, wctx, kSiteMmaTmemEmpty)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint64_t adesc = ptx::umma_desc_sw128(sA0 + s * Cfg::A_BYTES, 16, 1024);
-          const uint64_t bdesc = ptx::umma_desc_sw128(sB0 + s * Cfg::B_BYTES, BK * 128, 1024);
+          dtm = tmem_base + static_cast<uint32_t>(acc * BN);
+          for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            // A (K-major): +32 bytes per k16 inside the swizzle row. B (N-major): +16 rows
-            // of 128 bytes per k16. Descriptor start addresses are in 16-byte units.
-            ptx::umma_f16<PAIR>(dtm, adesc + static_cast<uint64_t>(2 * k),
-                                bdesc + static_cast<uint64_t>(128 * k), idesc,
-                                (kb | k) != 0 ? 1u : 0u);
+            for (int j = 0; j < Cfg::N_SUB; ++j) issue_sub(s, kb, j);
+            release_stage(s);
+            if (++s == S) {
+              s = 0;
+              ph ^= 1u;
+            }
           }
-          issued_any = true;
-          const uint32_t eb = ptx::smem_u32(&empty[s]);
-          if (PAIR == 2)
-            ptx::umma_commit_pair_mask(eb, 0x3);  // both CTAs' copies of empty[s]
-          else
-            ptx::umma_commit<1>(eb);
-          if (++s == S) {
-            s = 0;
-            ph ^= 1u;
+        } else {
+          // One accumulator; the epilogue hands its two N halves back separately
+          // (tempty[0], tempty[1]). As soon as half 0 is free this tile's UMMAs for N-slice 0
+          // run ahead by up to S stages while half 1 still drains; slice-1 UMMAs of those
+          // stages follow (in k order) once half 1 is free, and only then are the stages
+          // released to the producer.
+          dtm = tmem_base;
+          if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[0]), aph ^ 1u, wctx, kSiteMmaTmemEmpty)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          bool h1 = false;
+          int pend_s = 0, pend_kb = 0, npend = 0;
+          auto flush = [&]() {
+            for (int q = 0; q < npend; ++q) {
+              const int st = (pend_s + q) % S;
+              issue_sub(st, pend_kb + q, 1);
+              release_stage(st);
+            }
+            npend = 0;
+          };
+          for (int kb = 0; kb < p.num_kb; ++kb) {
+            if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            issue_sub(s, kb, 0);
+            if (!h1 && ptx::mbar_test_wait_cluster(ptx::smem_u32(&tempty[1]), aph ^ 1u)) {
+              ptx::tc_fence_after();
+              h1 = true;
+            }
+            if (h1) {
+              flush();
+              issue_sub(s, kb, 1);
+              release_stage(s);
+            } else {
+              if (npend == 0) {
+                pend_s = s;
+                pend_kb = kb;
+              }
+              if (++npend == S) {
+                if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[1]), aph ^ 1u, wctx,
+                                         kSiteMmaTmemEmpty)) {
+                  ok = false;
+                  break;
+                }
+                ptx::tc_fence_after();
+                h1 = true;
+                flush();
+              }
+            }
+            if (++s == S) {
+              s = 0;
+              ph ^= 1u;
+            }
+          }
+          if (ok && !h1) {
+            if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[1]), aph ^ 1u, wctx, kSiteMmaTmemEmpty)) {
+              ok = false;
+            } else {
+              ptx::tc_fence_after();
+              flush();
+            }
           }
         }
         if (!ok) break;
@@ -329,6 +548,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ptx::umma_commit_pair_mask(fb, 0x3);
         else
           ptx::umma_commit<1>(fb);
+        ++it;
       }
       if (!ok && issued_any) {
         // Unwinding: every UMMA this thread issued must retire before TMEM is freed.
@@ -350,24 +570,75 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float alpha = p.alpha, beta = p.beta;
     int it = 0;
     int chunk_ctr = 0;
-    for (int t = cid; t < p.num_tiles; t += ncl, ++it) {
-      const int acc = it & 1;
-      const uint32_t aph = static_cast<uint32_t>(it >> 1) & 1u;
-      // One lane waits; the result is broadcast so the warp stays converged for the
-      // .sync.aligned TMEM loads below.
-      int ok = 1;
-      if (lane == 0)
-        ok = wait_bar<PAIR == 2>(ptx::smem_u32(&tfull[acc]), aph, wctx, kSiteEpiTmemFull) ? 1 : 0;
+    int sslot = 0;
+    uint32_t sph = 0;
+    for (;;) {
+      // One lane takes the tile index and waits for the accumulator; the results are
+      // broadcast so the warp stays converged for the .sync.aligned TMEM loads below.
+      int ok = 1, tile = -1;
+      const int acc = it % ACC_BUFS;
+      const uint32_t aph = static_cast<uint32_t>(it / ACC_BUFS) & 1u;
+      if (lane == 0) {
+        ok = sched_read(sslot, sph, tile) ? 1 : 0;
+        if (ok && tile >= 0)
+          ok = wait_bar<PAIR == 2>(ptx::smem_u32(&tfull[acc]), aph, wctx, kSiteEpiTmemFull) ? 1 : 0;
+      }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      tile = __shfl_sync(0xffffffffu, tile, 0);
+      if (!ok || tile < 0) break;
       ptx::tc_fence_after();
       int tm, tn;
-      decode_tile(t, p, tm, tn);
+      decode_tile(tile, p, tm, tn);
       const int row0 = tm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M + EPI_ROWS * q;
       const int col0 = tn * BN;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(EPI_ROWS * q) << 16) + static_cast<uint32_t>(acc * BN);
       const int r = row0 + lane;  // this thread's output row
+      if constexpr (ACC_BUFS == 1 && TMA_EPI) {
+        if (beta == 0.0f) {
+          // Single accumulator: drain each N half into registers as packed halves, give that
+          // half of TMEM back at once, then store it with 16-byte stores (row per thread).
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            uint32_t P[128];
+#pragma unroll
+            for (int q8 = 0; q8 < 8; ++q8) {
+              uint32_t v[32];
+              ptx::tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(h * (BN / 2) + q8 * 32), v);
+              ptx::tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                P[q8 * 16 + i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
+                                            alpha * __uint_as_float(v[2 * i + 1]));
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              const uint32_t tb = tempty_leader + static_cast<uint32_t>(h) * 8u;
+              if (PAIR == 2)
+                ptx::mbar_arrive_cluster(tb);
+              else
+                ptx::mbar_arrive(tb);
+            }
+            if (r < p.M) {
+              __half *crow = p.C + static_cast<long long>(r) * p.N + col0 + h * (BN / 2);
+#pragma unroll
+              for (int g = 0; g < (BN / 2) / 8; ++g) {
+                if (col0 + h * (BN / 2) + 8 * g < p.N) {  // N % 8 == 0: whole 16-byte groups
+                  uint4 w;
+                  w.x = P[4 * g + 0];
+                  w.y = P[4 * g + 1];
+                  w.z = P[4 * g + 2];
+                  w.w = P[4 * g + 3];
+                  *reinterpret_cast<uint4 *>(crow + 8 * g) = w;
+                }
+              }
+            }
+          }
+          ++it;
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / EPI_COLS; ++c, ++chunk_ctr) {
         uint32_t v[64];
@@ -375,12 +646,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
                                 *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         ptx::tmem_ld_wait();
-        if (c == BN / EPI_COLS - 1) {
-          // Whole accumulator read: hand the buffer back to the UMMA issuer.
+        // Accumulator (or, with one accumulator, one N half of it) fully read: hand it back
+        // to the UMMA issuer.
+        const bool last_of_half = (ACC_BUFS == 1) && (c == BN / EPI_COLS / 2 - 1);
+        if (c == BN / EPI_COLS - 1 || last_of_half) {
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) {
-            const uint32_t tb = tempty_leader + static_cast<uint32_t>(acc) * 8u;
+            const int which = (ACC_BUFS == 1) ? (last_of_half ? 0 : 1) : acc;
+            const uint32_t tb = tempty_leader + static_cast<uint32_t>(which) * 8u;
             if (PAIR == 2)
               ptx::mbar_arrive_cluster(tb);
             else
@@ -484,6 +758,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+      ++it;
     }
     if (TMA_EPI && lane == 0) ptx::bulk_wait_group<0>();
     __syncwarp();
@@ -637,22 +912,32 @@ bool encode_2d(CUtensorMap *map, const void *ptr, int rows, int cols, long long 
 }
 
 // ---------------------------------------------------------------- kernel table
-enum TileId { kT256x256 = 0, kT256x128 = 1, kT128x256 = 2, kT128x128 = 3, kT128x64 = 4, kNumTiles = 5 };
+enum TileId {
+  kT256x512 = 0,
+  kT256x256 = 1,
+  kT256x128 = 2,
+  kT128x256 = 3,
+  kT128x128 = 4,
+  kT128x64 = 5,
+  kNumTiles = 6
+};
 struct TileInfo {
-  int pair, bn, stages, smem;
+  int pair, bn, stages, smem, acc_bufs;
 };
 constexpr TileInfo kTiles[kNumTiles] = {
-    {2, 256, TileCfg<2, 256>::STAGES, TileCfg<2, 256>::SMEM},
-    {2, 128, TileCfg<2, 128>::STAGES, TileCfg<2, 128>::SMEM},
-    {1, 256, TileCfg<1, 256>::STAGES, TileCfg<1, 256>::SMEM},
-    {1, 128, TileCfg<1, 128>::STAGES, TileCfg<1, 128>::SMEM},
-    {1, 64, TileCfg<1, 64>::STAGES, TileCfg<1, 64>::SMEM},
+    {2, 512, TileCfg<2, 512>::STAGES, TileCfg<2, 512>::SMEM, TileCfg<2, 512>::ACC_BUFS},
+    {2, 256, TileCfg<2, 256>::STAGES, TileCfg<2, 256>::SMEM, TileCfg<2, 256>::ACC_BUFS},
+    {2, 128, TileCfg<2, 128>::STAGES, TileCfg<2, 128>::SMEM, TileCfg<2, 128>::ACC_BUFS},
+    {1, 256, TileCfg<1, 256>::STAGES, TileCfg<1, 256>::SMEM, TileCfg<1, 256>::ACC_BUFS},
+    {1, 128, TileCfg<1, 128>::STAGES, TileCfg<1, 128>::SMEM, TileCfg<1, 128>::ACC_BUFS},
+    {1, 64, TileCfg<1, 64>::STAGES, TileCfg<1, 64>::SMEM, TileCfg<1, 64>::ACC_BUFS},
 };
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, KParams);
 
 KernelFn kernel_for(int tile, bool tma_epi) {
   switch (tile) {
+    case kT256x512: return tma_epi ? hgemm_tc_kernel<2, 512, true> : hgemm_tc_kernel<2, 512, false>;
     case kT256x256: return tma_epi ? hgemm_tc_kernel<2, 256, true> : hgemm_tc_kernel<2, 256, false>;
     case kT256x128: return tma_epi ? hgemm_tc_kernel<2, 128, true> : hgemm_tc_kernel<2, 128, false>;
     case kT128x256: return tma_epi ? hgemm_tc_kernel<1, 256, true> : hgemm_tc_kernel<1, 256, false>;
@@ -662,11 +947,8 @@ KernelFn kernel_for(int tile, bool tma_epi) {
 }
 
 int tile_from_force(int force_bm, int force_bn) {
-  if (force_bm == 256 && force_bn == 256) return kT256x256;
-  if (force_bm == 256 && force_bn == 128) return kT256x128;
-  if (force_bm == 128 && force_bn == 256) return kT128x256;
-  if (force_bm == 128 && force_bn == 128) return kT128x128;
-  if (force_bm == 128 && force_bn == 64) return kT128x64;
+  for (int t = 0; t < kNumTiles; ++t)
+    if (force_bm == CTA_M * kTiles[t].pair && force_bn == kTiles[t].bn) return t;
   return -1;
 }
 
@@ -771,9 +1053,9 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   int tile = tile_from_force(force_bm, force_bn);
   if (tile < 0) {
     // Preference order on ties: least operand traffic per flop first.
-    const int order[kNumTiles] = {kT256x256, kT256x128, kT128x256, kT128x128, kT128x64};
+    const int order[] = {kT256x256, kT256x128, kT128x256, kT128x128, kT128x64};
     long long best = -1;
-    for (int o = 0; o < kNumTiles; ++o) {
+    for (int o = 0; o < static_cast<int>(sizeof(order) / sizeof(order[0])); ++o) {
       const TileInfo &ti = kTiles[order[o]];
       const long long tiles =
           static_cast<long long>(ceil_div(M, CTA_M * ti.pair)) * ceil_div(N, ti.bn);
@@ -797,7 +1079,8 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   const long long total = static_cast<long long>(pl->tiles_m) * pl->tiles_n;
   const int slots = ti.pair == 2 ? pair_slots : sm_count;
   const int units = static_cast<int>(std::min<long long>(total, slots));
-  pl->grid_ctas = units * ti.pair;
+  // One cluster per tile; the running ones take over the rest (cluster launch control).
+  pl->grid_ctas = static_cast<int>(total * ti.pair);
   if (group_m == 0) {
     // Working set of one wave ~ g tile-rows of A plus (units/g) tile-columns of B; choose g
     // near sqrt(units * tile_n / tile_m) (equal A and B footprints), at least 1.
@@ -1009,8 +1292,11 @@ int hgemm_launch_tuned(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_
     cudaEvent_t e0, e1;
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
-    const int bms[kNumTiles] = {256, 256, 128, 128, 128};
-    const int bns[kNumTiles] = {256, 128, 256, 128, 64};
+    int bms[kNumTiles], bns[kNumTiles];
+    for (int t = 0; t < kNumTiles; ++t) {
+      bms[t] = CTA_M * kTiles[t].pair;
+      bns[t] = kTiles[t].bn;
+    }
     const int gms[5] = {0, 4, 8, 16, 32};
     float best_ms = 1e30f;
     for (int t = 0; t < kNumTiles; ++t) {

@@ -71,14 +71,17 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
                : "memory");
 }
+// Potentially blocking test: the thread may be suspended in hardware for up to
+// `kSuspendNs` (it resumes as soon as the phase completes), so waiting threads do not spin.
+constexpr uint32_t kSuspendNs = 100000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -87,7 +90,19 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+// Non-blocking test (never suspends), cluster-scope acquire.
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -106,6 +121,40 @@ __device__ __forceinline__ void cluster_wait() {
 __device__ __forceinline__ void cluster_sync() {
   cluster_arrive();
   cluster_wait();
+}
+
+// 32-bit store into the shared memory of a CTA of this cluster (address from mapa).
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr_cluster, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr_cluster), "r"(v) : "memory");
+}
+
+// ------------------------------------------------------------------------ cluster launch control
+// Ask the hardware to cancel the launch of one not-yet-running cluster of this grid; the
+// 16-byte response lands in this CTA's shared memory at `resp` and completes 16 transaction
+// bytes on `bar` (which the caller arms with expect_tx). Only this CTA receives the response.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128"
+      " [%0], [%1];" ::"r"(resp),
+      "r"(bar)
+      : "memory");
+}
+// Decodes a response: returns true and the first ctaid.x of the cancelled cluster, or false
+// when no cluster was left to cancel.
+__device__ __forceinline__ bool clc_query(uint32_t resp, uint32_t &first_ctaid_x) {
+  uint32_t ok, x;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b128 r;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "mov.u32 %1, 0;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}"
+      : "=r"(ok), "=r"(x)
+      : "r"(resp)
+      : "memory");
+  first_ctaid_x = x;
+  return ok != 0;
 }
 
 // ------------------------------------------------------------------------ TMA

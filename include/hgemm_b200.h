@@ -60,9 +60,9 @@ int hgemm_launch(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, 
                  int K, float alpha, float beta, hgemm_stream_t stream);
 
 /* Same, with the reference's override knobs. force_bm in {0, 128, 256} (256 = a 2-SM
- * UMMA pair of two 128-row CTAs), force_bn in {0, 64, 128, 256}; 0 means automatic.
- * Valid explicit tiles: 256x256, 256x128, 128x256, 128x128, 128x64. group_m = raster band
- * height in tile rows (0 = automatic). */
+ * UMMA pair of two 128-row CTAs), force_bn in {0, 64, 128, 256, 512}; 0 means automatic.
+ * Valid explicit tiles: 256x512, 256x256, 256x128, 128x256, 128x128, 128x64.
+ * group_m = raster band height in tile rows (0 = automatic). */
 int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N,
                     int K, float alpha, float beta, hgemm_stream_t stream, int force_bm,
                     int force_bn, int group_m);
@@ -103,7 +103,8 @@ typedef struct {
   int group_m;    /* raster band height in tile rows */
   int stages;     /* smem pipeline depth */
   int tiles_m, tiles_n;
-  int grid_ctas;  /* persistent CTAs launched */
+  int grid_ctas;  /* CTAs launched: one cluster of `pair` CTAs per tile; running clusters
+                     take over not-yet-started ones (cluster launch control) */
   int pad_a, pad_b;      /* operand restrided into scratch (K % 8, N % 8) */
   int lda, ldb;          /* leading dimensions the tensor maps use */
   int tma_store;         /* 1: TMA-store epilogue (N % 8 == 0), 0: SIMT stores */

@@ -16,7 +16,7 @@ from tests.gpu_util import cublas, dev, hash_fill_, host, rel_l2
 
 pytestmark = pytest.mark.gpu
 
-TILES = [(256, 256), (256, 128), (128, 256), (128, 128), (128, 64)]
+TILES = [(256, 512), (256, 256), (256, 128), (128, 256), (128, 128), (128, 64)]
 
 
 def run(hg, A, B, C, alpha, beta, via="solve", force=(0, 0), nan_c=False):
