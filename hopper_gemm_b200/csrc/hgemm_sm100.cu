@@ -600,17 +600,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // half of TMEM back at once, then store it with 16-byte stores (row per thread).
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
+            // Two batches of four 32-column TMEM loads, one wait each; the half goes back to
+            // the UMMA issuer right after the second wait, before any conversion or store.
+            const uint32_t ta = tbase + static_cast<uint32_t>(h * (BN / 2));
             uint32_t P[128];
+            uint32_t v[128];
 #pragma unroll
-            for (int q8 = 0; q8 < 8; ++q8) {
-              uint32_t v[32];
-              ptx::tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(h * (BN / 2) + q8 * 32), v);
-              ptx::tmem_ld_wait();
+            for (int b = 0; b < 4; ++b)
+              ptx::tmem_ld_32x32b_x32(ta + 32 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * b]));
+            ptx::tmem_ld_wait();
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                P[q8 * 16 + i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
-                                            alpha * __uint_as_float(v[2 * i + 1]));
-            }
+            for (int i = 0; i < 64; ++i)
+              P[i] = pack_half2(alpha * __uint_as_float(v[2 * i]), alpha * __uint_as_float(v[2 * i + 1]));
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+              ptx::tmem_ld_32x32b_x32(ta + 128 + 32 * b,
+                                      *reinterpret_cast<uint32_t(*)[32]>(&v[32 * b]));
+            ptx::tmem_ld_wait();
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -620,6 +626,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               else
                 ptx::mbar_arrive(tb);
             }
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              P[64 + i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
+                                     alpha * __uint_as_float(v[2 * i + 1]));
             if (r < p.M) {
               __half *crow = p.C + static_cast<long long>(r) * p.N + col0 + h * (BN / 2);
 #pragma unroll
@@ -1403,3 +1413,4 @@ int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int
 }
 
 }  // extern "C"
+
