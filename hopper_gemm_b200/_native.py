@@ -45,6 +45,8 @@ SIGNATURES = {
     "hgemm_launch": (_i, _GEMM + [_vp]),
     "hgemm_launch_ex": (_i, _GEMM + [_vp, _i, _i, _i]),
     "hgemm_launch_tuned": (_i, _GEMM + [_vp]),
+    "hgemm_launch_noalloc": (_i, _GEMM + [_vp]),
+    "hgemm_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "hgemm_last_status": (_i, []),
     "hgemm_status_string": (ctypes.c_char_p, [_i]),
     "hgemm_device_status": (_i, [_i, ctypes.POINTER(_i)]),

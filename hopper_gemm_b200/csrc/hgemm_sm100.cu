@@ -1414,3 +1414,101 @@ int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int
 
 }  // extern "C"
 
+// ============================================================================ no-allocation entry
+// Some callers cannot allocate device memory when they call the GEMM: a host that owns a
+// fixed device-memory pool and forbids anything else to call cudaMalloc, a process whose
+// caller-facing path must not take the allocator's lock or implicitly synchronise the
+// device (cudaMalloc/cudaFree may do both), or code with a strict memory budget decided
+// ahead of time. hgemm_launch_noalloc serves them: it is hgemm_launch, except that the one
+// scratch buffer the path can need -- the restrided copy of A when K % 8 != 0 and of B when
+// N % 8 != 0 -- lives in the fixed-size array below, which the library's module owns on
+// every device that loads it (until the process exits), instead of coming from cudaMalloc.
+namespace hgemm {
+namespace {
+
+constexpr size_t kNoallocScratchBytes = 64ull << 20;  // 64 MiB
+
+// Device-side storage. Host code never uses this name as an address: the host-side symbol
+// is only a stand-in, and a kernel handed it would fault (or quietly touch host memory).
+// The real device address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[64] = {};
+
+// Caller holds g_noalloc_mu; `dev` is current.
+int noalloc_scratch(int dev, __half **out) {
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return HGEMM_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = static_cast<__half *>(g_noalloc_ptr[dev]);
+  return HGEMM_OK;
+}
+
+int launch_noalloc_impl(const __half *A, const __half *B, __half *C, int M, int N, int K,
+                        float alpha, float beta, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return HGEMM_OK;
+  if (!A || !B || !C) return HGEMM_ERR_INVALID_ARG;
+  int dev;
+  if (current_device(&dev) != HGEMM_OK) return HGEMM_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DevState *d = nullptr;
+  int st = ensure_device(dev, &d);
+  if (st != HGEMM_OK) return st;
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+  hgemm_plan_t pl;
+  st = make_plan(M, N, K, beta, aligned16, 0, 0, 0, d->sm_count, d->pair_slots, &pl);
+  if (st != HGEMM_OK) return st;
+  if (pl.path == 0) return HGEMM_OK;
+  if (pl.path == 2) return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
+  const __half *Ause = A, *Buse = B;
+  if (pl.pad_a || pl.pad_b) {
+    if (pl.scratch_bytes > kNoallocScratchBytes) return HGEMM_ERR_TOO_LARGE;
+    __half *w = nullptr;
+    {
+      std::lock_guard<std::mutex> lk(g_noalloc_mu);
+      st = noalloc_scratch(dev, &w);
+    }
+    if (st != HGEMM_OK) return st;
+    // Nothing here has to start at zero: each element the GEMM reads from the array is
+    // written by the restride pass of this same call, earlier on the same stream.
+    const size_t na = pl.pad_a ? static_cast<size_t>(M) * pl.lda : 0;
+    if (pl.pad_a) {
+      st = launch_restride(A, w, M, K, pl.lda, d->sm_count, stream);
+      if (st != HGEMM_OK) return st;
+      Ause = w;
+    }
+    if (pl.pad_b) {
+      st = launch_restride(B, w + na, K, N, pl.ldb, d->sm_count, stream);
+      if (st != HGEMM_OK) return st;
+      Buse = w + na;
+    }
+  }
+  int tile = -1;
+  for (int t = 0; t < kNumTiles; ++t)
+    if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;
+  return launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, C, M, N, K, alpha, beta, stream, *d);
+}
+
+}  // namespace
+}  // namespace hgemm
+
+extern "C" {
+
+size_t hgemm_noalloc_scratch_bytes(void) { return hgemm::kNoallocScratchBytes; }
+
+int hgemm_launch_noalloc(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                         int N, int K, float alpha, float beta, hgemm_stream_t stream) {
+  return hgemm::set_status(hgemm::launch_noalloc_impl(
+      A, B, C, M, N, K, alpha, beta, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

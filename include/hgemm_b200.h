@@ -72,6 +72,24 @@ int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *
 int hgemm_launch_tuned(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
                        int N, int K, float alpha, float beta, hgemm_stream_t stream);
 
+/* No-allocation variant of hgemm_launch (no counterpart in the reference). For callers
+ * that must not allocate device memory at call time -- a framework that owns a fixed
+ * device-memory pool and forbids other cudaMalloc calls, or a latency-critical path that
+ * cannot take the allocator's lock or its implicit device synchronisation. The only scratch
+ * the GEMM can need (the restrided copy of A when K % 8 != 0 and of B when N % 8 != 0) comes
+ * from a fixed array of hgemm_noalloc_scratch_bytes() (64 MiB) that the library keeps on every
+ * device that loads it, until the process exits; no cudaMalloc/cudaFree happens here.
+ * Shapes whose restrided operands need more return HGEMM_ERR_TOO_LARGE before any work.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call outside any stream capture. Each device has
+ * its own copy of the array, and every call on a device shares that copy and leaves its
+ * contents behind: two calls on one device that can overlap on the GPU (different streams)
+ * race on it when both need restriding, so order them. Same arguments, semantics and status
+ * codes as hgemm_launch. */
+int hgemm_launch_noalloc(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                         int N, int K, float alpha, float beta, hgemm_stream_t stream);
+size_t hgemm_noalloc_scratch_bytes(void);
+
 /* ---------------------------------------------------------------- status, planning */
 
 /* Status of the last call made by this host thread. */
