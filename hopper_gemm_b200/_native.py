@@ -59,6 +59,9 @@ SIGNATURES = {
     "hgemm_comm_destroy": (_i, [_vp]),
     "hgemm_sharded_rank": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _f, _i, _vp]),
     "hgemm_shard_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "hgemm_shard_chunk_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "hgemm_comm_check": (_i, [_vp]),
+    "hgemm_comm_abort": (_i, [_vp]),
 }
 
 

@@ -145,6 +145,36 @@ int hgemm_comm_destroy(hgemm_comm_t c) {
   return st;
 }
 
+int hgemm_comm_check(hgemm_comm_t c) {
+  if (!c) return HGEMM_ERR_INVALID_ARG;
+  const NcclApi &a = nccl();
+  if (!a.ok) return HGEMM_ERR_NCCL;
+  ncclResult_t r = ncclSuccess;
+  if (a.CommGetAsyncError(c->comm, &r) != ncclSuccess) return HGEMM_ERR_NCCL;
+  return (r == ncclSuccess || r == ncclInProgress) ? HGEMM_OK : HGEMM_ERR_NCCL;
+}
+
+int hgemm_comm_abort(hgemm_comm_t c) {
+  if (!c) return HGEMM_ERR_INVALID_ARG;
+  const NcclApi &a = nccl();
+  int st = HGEMM_OK;
+  if (c->comm && a.ok && a.CommAbort(c->comm) != ncclSuccess) st = HGEMM_ERR_NCCL;
+  c->comm = nullptr;
+  for (cudaEvent_t e : c->chunk_done) cudaEventDestroy(e);
+  if (c->gather_done) cudaEventDestroy(c->gather_done);
+  if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
+  delete c;
+  return st;
+}
+
+int hgemm_shard_chunk_rows(int rows, int chunks, int chunk, int *begin, int *count) {
+  if (rows < 0 || chunks <= 0 || chunk < 0 || chunk >= chunks || !begin || !count)
+    return HGEMM_ERR_INVALID_ARG;
+  *begin = static_cast<int>(static_cast<long long>(rows) * chunk / chunks);
+  *count = static_cast<int>(static_cast<long long>(rows) * (chunk + 1) / chunks) - *begin;
+  return HGEMM_OK;
+}
+
 int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_half_t *B,
                        hgemm_half_t *C, int M, int N, int K, float alpha, float beta, int chunks,
                        hgemm_stream_t stream) {
@@ -155,16 +185,15 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
   const int P = c->nranks, me = c->rank;
   int rb = 0, rc = 0;
   hgemm_shard_rows(M, P, me, &rb, &rc);
+  // Every rank must post the same sequence of collectives, so the chunk count may depend
+  // only on (M, P, chunks): at most the smallest rank's row count.
   if (chunks < 1) chunks = 1;
-  chunks = std::max(1, std::min(chunks, std::max(rc, 1)));
+  chunks = std::max(1, std::min(chunks, std::max(M / P, 1)));
   const size_t row_elems = static_cast<size_t>(N);
 
   // Rows [cb, cb + cn) of the rank-local block that make up chunk `ch`.
   auto chunk_rows = [&](int count, int ch, int *cb, int *cn) {
-    const long long b = static_cast<long long>(count) * ch / chunks;
-    const long long e = static_cast<long long>(count) * (ch + 1) / chunks;
-    *cb = static_cast<int>(b);
-    *cn = static_cast<int>(e - b);
+    hgemm_shard_chunk_rows(count, chunks, ch, cb, cn);
   };
 
   if (M % P == 0 && chunks == 1) {

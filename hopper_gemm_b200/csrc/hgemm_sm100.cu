@@ -145,15 +145,27 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Wa
 }
 
 __device__ __forceinline__ void decode_tile(int t, const KParams &p, int &tm, int &tn) {
-  // Bands of group_m tile-rows; inside a band the M index runs fastest, so the CTAs working
-  // at the same time share a few A row-blocks and B column-blocks in L2.
-  const int band_tiles = p.group_m * p.tiles_n;
-  const int band = t / band_tiles;
-  const int idx = t - band * band_tiles;
-  const int m0 = band * p.group_m;
-  const int rows = min(p.group_m, p.tiles_m - m0);
-  tm = m0 + idx % rows;
-  tn = idx / rows;
+  // Bands of |group_m| tile-rows (group_m > 0: M index fastest inside a band) or of
+  // |group_m| tile-columns (group_m < 0: N index fastest), so the tiles in flight at the
+  // same time share a few A row-blocks and B column-blocks in L2.
+  if (p.group_m > 0) {
+    const int band_tiles = p.group_m * p.tiles_n;
+    const int band = t / band_tiles;
+    const int idx = t - band * band_tiles;
+    const int m0 = band * p.group_m;
+    const int rows = min(p.group_m, p.tiles_m - m0);
+    tm = m0 + idx % rows;
+    tn = idx / rows;
+  } else {
+    const int g = -p.group_m;
+    const int band_tiles = g * p.tiles_m;
+    const int band = t / band_tiles;
+    const int idx = t - band * band_tiles;
+    const int n0 = band * g;
+    const int cols = min(g, p.tiles_n - n0);
+    tn = n0 + idx % cols;
+    tm = idx / cols;
+  }
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
@@ -1030,7 +1042,7 @@ int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b
 int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int force_bn,
               int group_m, int sm_count, int pair_slots, hgemm_plan_t *pl) {
   std::memset(pl, 0, sizeof(*pl));
-  if (M < 0 || N < 0 || K < 0 || group_m < 0) return HGEMM_ERR_INVALID_ARG;
+  if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
   if ((force_bm != 0 || force_bn != 0) && tile_from_force(force_bm, force_bn) < 0)
     return HGEMM_ERR_INVALID_ARG;
   if (sm_count <= 0) sm_count = 148;
@@ -1097,7 +1109,7 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
     const double g = std::sqrt(static_cast<double>(units) * pl->tile_n / pl->tile_m);
     group_m = std::max(1, static_cast<int>(g + 0.5));
   }
-  pl->group_m = std::min(group_m, pl->tiles_m);
+  pl->group_m = group_m > 0 ? std::min(group_m, pl->tiles_m) : -std::min(-group_m, pl->tiles_n);
   return HGEMM_OK;
 }
 

@@ -62,7 +62,8 @@ int hgemm_launch(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, 
 /* Same, with the reference's override knobs. force_bm in {0, 128, 256} (256 = a 2-SM
  * UMMA pair of two 128-row CTAs), force_bn in {0, 64, 128, 256, 512}; 0 means automatic.
  * Valid explicit tiles: 256x512, 256x256, 256x128, 128x256, 128x128, 128x64.
- * group_m = raster band height in tile rows (0 = automatic). */
+ * group_m = raster band height in tile rows, M index fastest inside a band (0 = automatic);
+ * a negative value -g selects bands of g tile columns with the N index fastest. */
 int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N,
                     int K, float alpha, float beta, hgemm_stream_t stream, int force_bm,
                     int force_bn, int group_m);
@@ -118,7 +119,7 @@ typedef struct {
   int tile_m;     /* rows per tile: 128 (one CTA) or 256 (2-SM pair) */
   int tile_n;     /* columns per tile */
   int pair;       /* 1 or 2 CTAs per UMMA */
-  int group_m;    /* raster band height in tile rows */
+  int group_m;    /* raster band: > 0 tile rows (M fastest), < 0 tile columns (N fastest) */
   int stages;     /* smem pipeline depth */
   int tiles_m, tiles_n;
   int grid_ctas;  /* CTAs launched: one cluster of `pair` CTAs per tile; running clusters
@@ -156,6 +157,14 @@ int hgemm_sharded_rank(hgemm_comm_t comm, const hgemm_half_t *A_local, const hge
 
 /* Row range helper, identical to the one hgemm_sharded_rank uses. */
 int hgemm_shard_rows(int M, int nranks, int rank, int *row_begin, int *row_count);
+/* Rows [begin, begin + count) of a `rows`-row block that form chunk `chunk` of `chunks`. */
+int hgemm_shard_chunk_rows(int rows, int chunks, int chunk, int *begin, int *count);
+
+/* HGEMM_OK while the communicator is healthy, HGEMM_ERR_NCCL once NCCL reports an
+ * asynchronous error (e.g. a peer died); poll it between steps. */
+int hgemm_comm_check(hgemm_comm_t comm);
+/* Tears the communicator down without waiting for peers (after a failure); frees `comm`. */
+int hgemm_comm_abort(hgemm_comm_t comm);
 
 #ifdef __cplusplus
 }
