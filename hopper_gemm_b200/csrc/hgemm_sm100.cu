@@ -130,7 +130,9 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Wa
   auto probe = [&]() {
     return CLUSTER_ACQ ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity);
   };
-  if (probe()) return true;
+  // Fast path first: a non-suspending test costs ~30 cycles less than try_wait when the
+  // phase is already complete, which is the common case on the UMMA issuer's hot loop.
+  if (ptx::mbar_test_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = ptx::globaltimer();
   for (uint32_t n = 1;; ++n) {
     if (probe()) return true;
@@ -269,19 +271,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // Readers take tile indices in ring order and release each slot to the leader's producer.
   const uint32_t sched_empty_leader0 =
       (PAIR == 2) ? ptx::mapa(ptx::smem_u32(&sched_empty[0]), 0u) : ptx::smem_u32(&sched_empty[0]);
-  auto sched_read = [&](int &slot, uint32_t &sph, int &tile) -> bool {
-    if (!wait_bar<PAIR == 2>(ptx::smem_u32(&sched_full[slot]), sph, wctx, kSiteSchedFull))
-      return false;
+  auto sched_take = [&](int &slot, uint32_t &sph, int &tile) {
     tile = sched_val[slot];
     const uint32_t eb = sched_empty_leader0 + static_cast<uint32_t>(slot) * 8u;
     if (PAIR == 2)
-      ptx::mbar_arrive_cluster(eb);
+      ptx::mbar_arrive_remote(eb);
     else
       ptx::mbar_arrive(eb);
     if (++slot == NSL) {
       slot = 0;
       sph ^= 1u;
     }
+  };
+  auto sched_read = [&](int &slot, uint32_t &sph, int &tile) -> bool {
+    if (!wait_bar<PAIR == 2>(ptx::smem_u32(&sched_full[slot]), sph, wctx, kSiteSchedFull))
+      return false;
+    sched_take(slot, sph, tile);
+    return true;
+  };
+  // Non-blocking: takes the next index only if it is already there.
+  auto sched_try_read = [&](int &slot, uint32_t &sph, int &tile) -> bool {
+    if (!ptx::mbar_test_wait_cluster(ptx::smem_u32(&sched_full[slot]), sph)) return false;
+    sched_take(slot, sph, tile);
     return true;
   };
 
@@ -457,13 +468,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         else
           ptx::umma_commit<1>(eb);
       };
-      while (ok) {
-        int tile = -1;
-        if (!sched_read(sslot, sph, tile)) {
-          ok = false;
-          break;
-        }
-        if (tile < 0) break;
+      // The issuer only needs to know whether another tile follows; it takes that index
+      // without blocking during the current tile's last S k-blocks (the producer publishes it
+      // once it has issued this tile's loads), so a tile start never waits on the ring.
+      int tile = -1;
+      if (!sched_read(sslot, sph, tile)) ok = false;
+      while (ok && tile >= 0) {
+        int next = -1;
+        bool have_next = false;
+        auto poll_next = [&](int kb) {
+          if (!have_next && kb >= p.num_kb - S && sched_try_read(sslot, sph, next)) have_next = true;
+        };
         const int acc = it % ACC_BUFS;
         const uint32_t aph = static_cast<uint32_t>(it / ACC_BUFS) & 1u;
         if constexpr (ACC_BUFS == 2) {
@@ -473,11 +488,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           ptx::tc_fence_after();
           dtm = tmem_base + static_cast<uint32_t>(acc * BN);
-          for (int kb = 0; kb < p.num_kb; ++kb) {
-            if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) {
-              ok = false;
-              break;
-            }
+          // One issuing thread has only ~4 UMMAs' time (BN=256) per k-block, so the hot loop
+          // carries nothing but the wait, the UMMAs and the stage release; the look-ahead on
+          // the tile ring happens in a separate tail loop over the last S k-blocks.
+          const int main_kb = p.num_kb > S ? p.num_kb - S : 0;
+          auto kblock = [&](int kb) -> bool {
+            if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) return false;
             ptx::tc_fence_after();
 #pragma unroll
             for (int j = 0; j < Cfg::N_SUB; ++j) issue_sub(s, kb, j);
@@ -486,13 +502,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               s = 0;
               ph ^= 1u;
             }
+            return true;
+          };
+          for (int kb = 0; kb < main_kb && ok; ++kb) ok = kblock(kb);
+          for (int kb = main_kb; kb < p.num_kb && ok; ++kb) {
+            ok = kblock(kb);
+            poll_next(kb);
           }
         } else {
-          // One accumulator; the epilogue hands its two N halves back separately
-          // (tempty[0], tempty[1]). As soon as half 0 is free this tile's UMMAs for N-slice 0
-          // run ahead by up to S stages while half 1 still drains; slice-1 UMMAs of those
-          // stages follow (in k order) once half 1 is free, and only then are the stages
-          // released to the producer.
+          // One accumulator of two N halves, each handed back separately by the epilogue
+          // (tempty[0], tempty[1]) and each announced separately to it (tfull[0], tfull[1]).
+          //  * Tile start: as soon as half 0 is free, N-slice-0 UMMAs run ahead by up to S
+          //    stages while half 1 still drains; the slice-1 UMMAs of those stages follow in
+          //    k order once half 1 is free, and only then are the stages released.
+          //  * Tile end: for the last S k-blocks the slice-0 UMMAs go first and tfull[0] is
+          //    committed before the slice-1 UMMAs, so the epilogue drains half 0 while the
+          //    tensor core still works on half 1 and the next tile can start on half 0
+          //    without the pipe running dry.
           dtm = tmem_base;
           if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[0]), aph ^ 1u, wctx, kSiteMmaTmemEmpty)) {
             ok = false;
@@ -509,6 +535,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             npend = 0;
           };
+          auto wait_h1 = [&]() -> bool {
+            if (h1) return true;
+            if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[1]), aph ^ 1u, wctx, kSiteMmaTmemEmpty))
+              return false;
+            ptx::tc_fence_after();
+            h1 = true;
+            return true;
+          };
+          const int tail_from = p.num_kb - S;  // k-blocks at or past this one are skewed
           for (int kb = 0; kb < p.num_kb; ++kb) {
             if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) {
               ok = false;
@@ -520,7 +555,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               ptx::tc_fence_after();
               h1 = true;
             }
-            if (h1) {
+            if (h1 && kb < tail_from) {
               flush();
               issue_sub(s, kb, 1);
               release_stage(s);
@@ -530,36 +565,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 pend_kb = kb;
               }
               if (++npend == S) {
-                if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[1]), aph ^ 1u, wctx,
-                                         kSiteMmaTmemEmpty)) {
+                // Every stage holds slice-0 work only; the producer needs one back.
+                if (!wait_h1()) {
                   ok = false;
                   break;
                 }
-                ptx::tc_fence_after();
-                h1 = true;
                 flush();
               }
             }
+            poll_next(kb);
             if (++s == S) {
               s = 0;
               ph ^= 1u;
             }
           }
-          if (ok && !h1) {
-            if (!wait_bar<PAIR == 2>(ptx::smem_u32(&tempty[1]), aph ^ 1u, wctx, kSiteMmaTmemEmpty)) {
-              ok = false;
-            } else {
-              ptx::tc_fence_after();
-              flush();
-            }
+          if (!ok) break;
+          {
+            const uint32_t fb0 = ptx::smem_u32(&tfull[0]);
+            if (PAIR == 2)
+              ptx::umma_commit_pair_mask(fb0, 0x3);
+            else
+              ptx::umma_commit<1>(fb0);
           }
+          if (!wait_h1()) {
+            ok = false;
+            break;
+          }
+          flush();
+          const uint32_t fb1 = ptx::smem_u32(&tfull[1]);
+          if (PAIR == 2)
+            ptx::umma_commit_pair_mask(fb1, 0x3);
+          else
+            ptx::umma_commit<1>(fb1);
         }
         if (!ok) break;
-        const uint32_t fb = ptx::smem_u32(&tfull[acc]);
-        if (PAIR == 2)
-          ptx::umma_commit_pair_mask(fb, 0x3);
-        else
-          ptx::umma_commit<1>(fb);
+        if constexpr (ACC_BUFS == 2) {
+          const uint32_t fb = ptx::smem_u32(&tfull[acc]);
+          if (PAIR == 2)
+            ptx::umma_commit_pair_mask(fb, 0x3);
+          else
+            ptx::umma_commit<1>(fb);
+        }
+        if (!have_next && !sched_read(sslot, sph, next)) {
+          ok = false;
+          break;
+        }
+        tile = next;
         ++it;
       }
       if (!ok && issued_any) {
@@ -606,63 +657,102 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(EPI_ROWS * q) << 16) + static_cast<uint32_t>(acc * BN);
       const int r = row0 + lane;  // this thread's output row
+      // With one accumulator, half 1 is announced separately (tfull[1]) after half 0.
+      auto wait_half1 = [&]() -> bool {
+        int okk = 1;
+        if (lane == 0)
+          okk = wait_bar<PAIR == 2>(ptx::smem_u32(&tfull[1]), aph, wctx, kSiteEpiTmemFull) ? 1 : 0;
+        okk = __shfl_sync(0xffffffffu, okk, 0);
+        if (okk) ptx::tc_fence_after();
+        return okk != 0;
+      };
       if constexpr (ACC_BUFS == 1 && TMA_EPI) {
         if (beta == 0.0f) {
           // Single accumulator: drain each N half into registers as packed halves, give that
-          // half of TMEM back at once, then store it with 16-byte stores (row per thread).
+          // half of TMEM back at once, then store it through the swizzled staging buffers
+          // with TMA stores.
+          bool aborted = false;
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
-            // Two batches of four 32-column TMEM loads, one wait each; the half goes back to
-            // the UMMA issuer right after the second wait, before any conversion or store.
+            if (h == 1 && !wait_half1()) {
+              aborted = true;
+              break;
+            }
+            // Three batches of 32-column TMEM loads (128 + 64 + 64 columns), one wait each;
+            // the half goes back to the UMMA issuer right after the last wait, before the
+            // last conversion and any store.
             const uint32_t ta = tbase + static_cast<uint32_t>(h * (BN / 2));
             uint32_t P[128];
-            uint32_t v[128];
+            {
+              uint32_t v[128];
 #pragma unroll
-            for (int b = 0; b < 4; ++b)
-              ptx::tmem_ld_32x32b_x32(ta + 32 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * b]));
+              for (int b = 0; b < 4; ++b)
+                ptx::tmem_ld_32x32b_x32(ta + 32 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[32 * b]));
+              ptx::tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 64; ++i)
+                P[i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
+                                  alpha * __uint_as_float(v[2 * i + 1]));
+            }
+            uint32_t v[64];
+            ptx::tmem_ld_32x32b_x32(ta + 128, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+            ptx::tmem_ld_32x32b_x32(ta + 160, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
             ptx::tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              P[i] = pack_half2(alpha * __uint_as_float(v[2 * i]), alpha * __uint_as_float(v[2 * i + 1]));
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-              ptx::tmem_ld_32x32b_x32(ta + 128 + 32 * b,
-                                      *reinterpret_cast<uint32_t(*)[32]>(&v[32 * b]));
+            for (int i = 0; i < 32; ++i)
+              P[64 + i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
+                                     alpha * __uint_as_float(v[2 * i + 1]));
+            ptx::tmem_ld_32x32b_x32(ta + 192, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+            ptx::tmem_ld_32x32b_x32(ta + 224, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
             ptx::tmem_ld_wait();
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) {
               const uint32_t tb = tempty_leader + static_cast<uint32_t>(h) * 8u;
               if (PAIR == 2)
-                ptx::mbar_arrive_cluster(tb);
+                ptx::mbar_arrive_remote(tb);
               else
                 ptx::mbar_arrive(tb);
             }
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              P[64 + i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
+            for (int i = 0; i < 32; ++i)
+              P[96 + i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
                                      alpha * __uint_as_float(v[2 * i + 1]));
-            if (r < p.M) {
-              __half *crow = p.C + static_cast<long long>(r) * p.N + col0 + h * (BN / 2);
+            const uint32_t stg_base = ptx::smem_u32(stg0) + static_cast<uint32_t>(lane) * 128u;
+            const uint32_t sw = static_cast<uint32_t>(lane & 7);
 #pragma unroll
-              for (int g = 0; g < (BN / 2) / 8; ++g) {
-                if (col0 + h * (BN / 2) + 8 * g < p.N) {  // N % 8 == 0: whole 16-byte groups
-                  uint4 w;
-                  w.x = P[4 * g + 0];
-                  w.y = P[4 * g + 1];
-                  w.z = P[4 * g + 2];
-                  w.w = P[4 * g + 3];
-                  *reinterpret_cast<uint4 *>(crow + 8 * g) = w;
-                }
+            for (int ch = 0; ch < (BN / 2) / EPI_COLS; ++ch, ++chunk_ctr) {
+              const uint32_t buf = static_cast<uint32_t>(chunk_ctr & 1) * (EPI_ROWS * 128);
+              // The TMA store that used this staging buffer two chunks ago must have read it.
+              if (lane == 0) ptx::bulk_wait_group_read<1>();
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                ptx::st_shared_v4(stg_base + buf + ((static_cast<uint32_t>(j) ^ sw) << 4),
+                                  P[32 * ch + 4 * j + 0], P[32 * ch + 4 * j + 1],
+                                  P[32 * ch + 4 * j + 2], P[32 * ch + 4 * j + 3]);
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                const int ccol = col0 + h * (BN / 2) + ch * EPI_COLS;
+                if (row0 < p.M && ccol < p.N)
+                  ptx::tma_store_2d(&tmC, ptx::smem_u32(stg0) + buf, ccol, row0);
+                ptx::bulk_commit_group();
               }
             }
           }
+          if (aborted) break;
           ++it;
           continue;
         }
       }
+      bool aborted_chunks = false;
 #pragma unroll 1
       for (int c = 0; c < BN / EPI_COLS; ++c, ++chunk_ctr) {
+        if (ACC_BUFS == 1 && c == BN / EPI_COLS / 2 && !wait_half1()) {
+          aborted_chunks = true;
+          break;
+        }
         uint32_t v[64];
         ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
@@ -678,7 +768,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int which = (ACC_BUFS == 1) ? (last_of_half ? 0 : 1) : acc;
             const uint32_t tb = tempty_leader + static_cast<uint32_t>(which) * 8u;
             if (PAIR == 2)
-              ptx::mbar_arrive_cluster(tb);
+              ptx::mbar_arrive_remote(tb);
             else
               ptx::mbar_arrive(tb);
           }
@@ -780,6 +870,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+      if (aborted_chunks) break;
       ++it;
     }
     if (TMA_EPI && lane == 0) ptx::bulk_wait_group<0>();
@@ -1074,20 +1165,30 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
 
   int tile = tile_from_force(force_bm, force_bn);
   if (tile < 0) {
-    // Preference order on ties: least operand traffic per flop first.
-    const int order[] = {kT256x256, kT256x128, kT128x256, kT128x128, kT128x64};
-    long long best = -1;
-    for (int o = 0; o < static_cast<int>(sizeof(order) / sizeof(order[0])); ++o) {
-      const TileInfo &ti = kTiles[order[o]];
-      const long long tiles =
-          static_cast<long long>(ceil_div(M, CTA_M * ti.pair)) * ceil_div(N, ti.bn);
-      const long long slots = ti.pair == 2 ? pair_slots : sm_count;
-      const long long waves = (tiles + slots - 1) / slots;
-      // per-CTA critical path ~ waves x columns x (K + fixed per-tile overhead in k units)
-      const long long cost = waves * ti.bn * (static_cast<long long>(K) + 256);
+    // Makespan model for the dynamic (cluster-launch-control) schedule: every CTA computes
+    // 128 rows x BN columns per tile, so its time per tile ~ BN * (K + fixed per-tile cost);
+    // with T tiles over `slots` co-resident units the last one finishes after about
+    // T / slots + 1/2 tiles (one tile when T <= slots). Per-flop factors measured on B200:
+    // the 256x512 pair tile moves 25% fewer operand bytes per flop, which keeps clocks
+    // higher under the power cap; narrower tiles leave the single UMMA-issuing thread less
+    // slack per k-block; one-CTA tiles read twice the B bytes per flop of a pair.
+    struct Cand {
+      int tile;
+      double factor;
+    };
+    const Cand cands[] = {{kT256x512, 0.95}, {kT256x256, 1.00}, {kT256x128, 1.06},
+                          {kT128x256, 1.10}, {kT128x128, 1.15}, {kT128x64, 1.22}};
+    double best = -1.0;
+    for (const Cand &c : cands) {
+      const TileInfo &ti = kTiles[c.tile];
+      const double tiles =
+          static_cast<double>(ceil_div(M, CTA_M * ti.pair)) * ceil_div(N, ti.bn);
+      const double slots = ti.pair == 2 ? pair_slots : sm_count;
+      const double makespan = tiles <= slots ? 1.0 : tiles / slots + 0.5;
+      const double cost = makespan * ti.bn * (static_cast<double>(K) + 512.0) * c.factor;
       if (best < 0 || cost < best) {
         best = cost;
-        tile = order[o];
+        tile = c.tile;
       }
     }
   }

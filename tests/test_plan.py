@@ -33,10 +33,12 @@ def test_restride_and_epilogue_choice(M, N, K, pad_a, pad_b, tma):
     assert p["scratch_bytes"] == want
 
 
-def test_large_square_uses_pair_tile():
+def test_large_square_uses_widest_pair_tile():
+    # enough tiles to fill the machine several times: the 256x512 pair tile (fewest operand
+    # bytes per flop) is chosen
     p = hg.plan(8192, 8192, 8192, **B200)
-    assert (p["tile_m"], p["tile_n"], p["pair"]) == (256, 256, 2)
-    assert p["grid_ctas"] == 2 * 32 * 32 and p["stages"] >= 4
+    assert (p["tile_m"], p["tile_n"], p["pair"]) == (256, 512, 2)
+    assert p["grid_ctas"] == 2 * 32 * 16 and p["stages"] >= 4
     assert 1 <= p["group_m"] <= p["tiles_m"]
 
 
