@@ -46,6 +46,10 @@ def parse():
     ap.add_argument("--force-bm", type=int, default=0, help="tile rows (0 = automatic)")
     ap.add_argument("--force-bn", type=int, default=0, help="tile columns (0 = automatic)")
     ap.add_argument("--group-m", type=int, default=0, help="raster band height (0 = automatic)")
+    ap.add_argument("--grid", action="store_true",
+                    help="the reference's 31-shape grid (perf_shapes.h) plus the ragged and thin-K "
+                         "configs, one JSON line per shape, ours vs cuBLAS interleaved")
+    ap.add_argument("--grid-reps", type=int, default=25)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -231,8 +235,95 @@ def run_reference(args, rank, world):
                 "d2h_bytes_per_step": 0}}), flush=True)
 
 
+# perf_shapes.h:2-11 (the reference's 31-shape benchmark grid) and BASELINE.json configs.
+GRID_SHAPES = [
+    (2048, 2048, 2048), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384),
+    (8192, 8192, 1024), (8192, 8192, 2048), (8192, 8192, 4096), (8192, 8192, 16384),
+    (16384, 8192, 4096), (4096, 4096, 8192), (32768, 8192, 2048), (4096, 4096, 1024),
+    (8192, 1024, 8192), (8192, 4096, 8192), (4096, 8192, 8192), (16384, 4096, 8192),
+    (4096, 8192, 128), (4096, 8192, 256), (4096, 8192, 512), (4096, 8192, 1024),
+    (8192, 8192, 128), (16384, 8192, 128), (3000, 1000, 2000), (384, 2048, 2048),
+    (1024, 1024, 1024), (2048, 2048, 512), (4096, 512, 4096),
+    (4096, 4095, 4096), (2048, 2047, 2048), (4095, 4095, 4095), (1024, 1023, 1024),
+]
+GRID_RAGGED = [(4095, 4095, 4095), (4096, 4095, 4096), (2048, 2047, 2048), (3000, 1000, 2000)]
+
+
+def run_grid(args):
+    """Reference methodology per shape (three_way.cu): hash-filled A/B, 5 interleaved
+    warm-ups, then `reps` rounds of {3x L2 memset, event, one launch, event} for ours and for
+    cuBLAS; median TFLOPS and the median of per-round paired ratios. The ragged configs are
+    also run with alpha=1.5, beta=0.5."""
+    import torch
+    import hopper_gemm_b200 as hg
+    from hopper_gemm_b200._native import cublas_ref_lib
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    cub = cublas_ref_lib()
+    flush = torch.empty(3 * torch.cuda.get_device_properties(dev).L2_cache_size,
+                        dtype=torch.uint8, device=dev)
+    cases = [(M, N, K, 1.0, 0.0) for (M, N, K) in GRID_SHAPES]
+    cases += [(M, N, K, 1.5, 0.5) for (M, N, K) in GRID_RAGGED]
+    for i, (M, N, K, al, be) in enumerate(cases):
+        A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device=dev), 0x9E3779B9 ^ i)
+        B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device=dev), 0x85EBCA6B ^ i)
+        C = hash_fill_(torch.empty((M, N), dtype=torch.float16, device=dev), 0x1234 ^ i)
+        R = C.clone()
+        C0 = C.clone()
+
+        def ours():
+            st = hg.lib.hgemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, al, be, sptr)
+            if st != 0:
+                raise RuntimeError(hg.status_string(st))
+
+        def cbl():
+            cub.hgemm_cublas_ref(A.data_ptr(), B.data_ptr(), R.data_ptr(), M, N, K, al, be, sptr)
+
+        def sample(fn):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            flush.fill_(0x5A)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            return e0.elapsed_time(e1)
+
+        # correctness of this shape against cuBLAS from the same C input
+        C.copy_(C0)
+        R.copy_(C0)
+        ours()
+        cbl()
+        torch.cuda.synchronize()
+        l2 = float((C.float() - R.float()).norm() / (R.float().norm() + 1e-30))
+        for _ in range(5):
+            ours()
+            cbl()
+        torch.cuda.synchronize()
+        to, tc = [], []
+        for _ in range(args.grid_reps):
+            to.append(sample(ours))
+            tc.append(sample(cbl))
+        fl = 2.0 * M * N * K
+        plan = hg.plan(M, N, K, beta=be)
+        print(json.dumps({
+            "shape": f"{M}x{N}x{K}", "alpha": al, "beta": be,
+            "ours_tflops": fl / (statistics.median(to) * 1e-3) / 1e12,
+            "cublas_tflops": fl / (statistics.median(tc) * 1e-3) / 1e12,
+            "paired_ratio_median": statistics.median(c / o for o, c in zip(to, tc)),
+            "rel_l2_vs_cublas": l2, "tile": f"{plan['tile_m']}x{plan['tile_n']}",
+            "restride": bool(plan["pad_a"] or plan["pad_b"])}), flush=True)
+        del A, B, C, R, C0
+        torch.cuda.empty_cache()
+
+
 def main():
     args = parse()
+    if args.grid:
+        run_grid(args)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))
