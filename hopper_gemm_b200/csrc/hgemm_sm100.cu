@@ -2,11 +2,12 @@
 // fp32 accumulate. Kernel, per-shape dispatcher and the C ABI declared in hgemm_b200.h.
 //
 // Design (B200-first, not a translation of the reference's sm_90a wgmma kernel):
-//   * Persistent grid, one CTA per SM (~226 KB of shared memory each), optionally launched
+//   * One CTA per SM (~226 KB of shared memory each), optionally launched
 //     as 2-CTA clusters that act as one UMMA pair: `tcgen05.mma.cta_group::2` computes a
 //     256 x BN tile, each CTA holding 128 rows of A and BN/2 columns of B in its own smem.
-//     The pair shares B through the tensor core, which is what the reference bought with a
-//     TMA multicast of B (mma_half.cu:331-367). No multicast load is issued anywhere.
+//     The pair shares B through the tensor core, which is what the reference bought by
+//     broadcasting B across its cluster (mma_half.cu:331-367). Every TMA load here lands in
+//     the issuing CTA's own shared memory.
 //   * Warp roles: warp 0 = TMA producer (one lane), warp 1 = TMEM allocator + UMMA issuer
 //     (one lane of the pair's leader CTA), warps 2..5 = epilogue (TMEM lane quarters).
 //   * fp32 accumulators live in TMEM, double buffered (2 x BN columns), so the epilogue of
@@ -57,6 +58,8 @@ constexpr int EPI_COLS = 64;    // columns per epilogue chunk (one 128-byte swiz
 constexpr int NUM_THREADS = 192;
 constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in dynamic shared memory per block
 constexpr int BAR_BYTES = 512;
+// Tiles whose main loop is estimated shorter than this (cycles) use the static schedule.
+constexpr double kStaticTileCycles = 8192.0;
 
 // Device status word: 0, or kDevTimeout | where. Written once per failure (first wins).
 constexpr unsigned kDevTimeout = 0x100u;
@@ -107,6 +110,7 @@ struct KParams {
   float alpha, beta;
   __half *C;
   unsigned long long timeout_ns;
+  int sched_static;  // 1: cluster c takes tiles c, c + clusters, ...; 0: cluster launch control
 };
 
 // ============================================================================ device helpers
@@ -367,7 +371,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           return true;
         };
-        bool clc_live = true, clc_pending = false;
+        bool clc_live = p.sched_static == 0, clc_pending = false;
+        const int stride = (PAIR == 2) ? static_cast<int>(ptx::nclusters_x()) : static_cast<int>(gridDim.x);
         uint32_t clc_ph = 0;
         int tile = first_tile;
         ok = publish(tile);
@@ -383,7 +388,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           int next = -1;
-          if (clc_live) {
+          if (p.sched_static) {
+            next = tile + stride < p.num_tiles ? tile + stride : -1;
+          } else if (clc_live) {
             if (!wait_bar<false>(ptx::smem_u32(clc_bar), clc_ph, wctx, kSiteClc)) {
               ok = false;
               break;
@@ -635,6 +642,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int chunk_ctr = 0;
     int sslot = 0;
     uint32_t sph = 0;
+    int c_prefetched = -1;
+    // L2 prefetch of the C_in rows this warp will read for `tile` (TMA, no smem).
+    auto prefetch_c_rows = [&](int tile_idx) {
+      int ptm, ptn;
+      decode_tile(tile_idx, p, ptm, ptn);
+      const int prow = ptm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M + EPI_ROWS * q;
+      if (prow >= p.M) return;
+#pragma unroll 1
+      for (int c = 0; c < BN / EPI_COLS; ++c) {
+        const int pcol = ptn * BN + c * EPI_COLS;
+        if (pcol < p.N) ptx::tma_prefetch_l2_2d(&tmC, pcol, prow);
+      }
+    };
     for (;;) {
       // One lane takes the tile index and waits for the accumulator; the results are
       // broadcast so the warp stays converged for the .sync.aligned TMEM loads below.
@@ -654,9 +674,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       decode_tile(tile, p, tm, tn);
       const int row0 = tm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M + EPI_ROWS * q;
       const int col0 = tn * BN;
+      if (TMA_EPI && beta != 0.0f && lane == 0) {
+        // beta != 0: start bringing this warp's 32 rows of C_in into L2 now; for every tile
+        // after the first this was already asked for one tile ahead (below).
+        if (tile != c_prefetched) prefetch_c_rows(tile);
+        // ... and the next tile's, if its index is already in the ring (read, not taken).
+        if (ptx::mbar_test_wait_cluster(ptx::smem_u32(&sched_full[sslot]), sph)) {
+          const int nt = sched_val[sslot];
+          if (nt >= 0) {
+            prefetch_c_rows(nt);
+            c_prefetched = nt;
+          }
+        }
+      }
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(EPI_ROWS * q) << 16) + static_cast<uint32_t>(acc * BN);
-      const int r = row0 + lane;  // this thread's output row
       // With one accumulator, half 1 is announced separately (tfull[1]) after half 0.
       auto wait_half1 = [&]() -> bool {
         int okk = 1;
@@ -747,21 +779,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       bool aborted_chunks = false;
-#pragma unroll 1
-      for (int c = 0; c < BN / EPI_COLS; ++c, ++chunk_ctr) {
-        if (ACC_BUFS == 1 && c == BN / EPI_COLS / 2 && !wait_half1()) {
-          aborted_chunks = true;
-          break;
-        }
-        uint32_t v[64];
+      constexpr int NCH = BN / EPI_COLS;
+      const bool unit_alpha = (alpha == 1.0f);
+      // The TMEM loads run one chunk ahead of the conversion and the stores (tcgen05.wait::ld
+      // waits for every load issued before it, so the next chunk's loads go out only after
+      // this chunk's registers were consumed).
+      uint32_t v[64];
+      auto load_chunk = [&](int c) {
         ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
                                 *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      };
+      load_chunk(0);
+      // beta != 0 with TMA stores: C_in is read with coalesced 16-byte loads (lane l takes
+      // row 4i + l/8, 16-byte group l%8), one chunk ahead, and transposed through the
+      // staging buffer so that each lane gets its own row.
+      const bool c_in = TMA_EPI && beta != 0.0f;
+      uint4 cin[8];
+      auto load_c = [&](int c) {
+        const int gc = col0 + c * EPI_COLS + 8 * (lane & 7);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int gr = row0 + 4 * i + (lane >> 3);
+          if (gr < p.M && gc < p.N)
+            cin[i] = __ldg(reinterpret_cast<const uint4 *>(p.C + static_cast<long long>(gr) * p.N + gc));
+          else
+            cin[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      };
+      if (c_in) load_c(0);
+#pragma unroll 1
+      for (int c = 0; c < NCH; ++c, ++chunk_ctr) {
+        if (ACC_BUFS == 1 && c == NCH / 2) {
+          // Half 1 is announced separately; its first chunk could not be loaded ahead.
+          if (!wait_half1()) {
+            aborted_chunks = true;
+            break;
+          }
+          load_chunk(c);
+        }
         ptx::tmem_ld_wait();
-        // Accumulator (or, with one accumulator, one N half of it) fully read: hand it back
-        // to the UMMA issuer.
-        const bool last_of_half = (ACC_BUFS == 1) && (c == BN / EPI_COLS / 2 - 1);
-        if (c == BN / EPI_COLS - 1 || last_of_half) {
+        float f[64];
+        if (unit_alpha) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) f[i] = alpha * __uint_as_float(v[i]);
+        }
+        const bool last_of_half = (ACC_BUFS == 1) && (c == NCH / 2 - 1);
+        if (c == NCH - 1 || last_of_half) {
+          // Accumulator (or, with one accumulator, one N half of it) fully read: hand it
+          // back to the UMMA issuer.
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -772,31 +841,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             else
               ptx::mbar_arrive(tb);
           }
+        } else {
+          load_chunk(c + 1);
         }
         const int ccol = col0 + c * EPI_COLS;
         uint8_t *stg = stg0 + (chunk_ctr & 1) * (EPI_ROWS * 128);
-        float f[64];
-#pragma unroll
-        for (int i = 0; i < 64; ++i) f[i] = alpha * __uint_as_float(v[i]);
 
         if (TMA_EPI) {
           // The TMA store that used this staging buffer two chunks ago must have read it.
           if (lane == 0) ptx::bulk_wait_group_read<1>();
           __syncwarp();
-          if (beta != 0.0f && r < p.M) {
-            const __half *crow = p.C + static_cast<long long>(r) * p.N;
+          if (c_in) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<uint4 *>(stg + sw128_off(4 * i + (lane >> 3), lane & 7)) = cin[i];
+            __syncwarp();
+            if (c + 1 < NCH) load_c(c + 1);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const int cc = ccol + 8 * j;
-              if (cc < p.N) {  // N % 8 == 0: a 16-byte group is wholly inside or outside
-                const uint4 u = *reinterpret_cast<const uint4 *>(crow + cc);
-                const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+              // N % 8 == 0: a 16-byte group is wholly inside or outside C (zeros outside)
+              const uint4 u = *reinterpret_cast<const uint4 *>(stg + sw128_off(lane, j));
+              const __half2 *h = reinterpret_cast<const __half2 *>(&u);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 cf = __half22float2(h[e]);
-                  f[8 * j + 2 * e] = fmaf(beta, cf.x, f[8 * j + 2 * e]);
-                  f[8 * j + 2 * e + 1] = fmaf(beta, cf.y, f[8 * j + 2 * e + 1]);
-                }
+              for (int e = 0; e < 4; ++e) {
+                const float2 cf = __half22float2(h[e]);
+                f[8 * j + 2 * e] = fmaf(beta, cf.x, f[8 * j + 2 * e]);
+                f[8 * j + 2 * e + 1] = fmaf(beta, cf.y, f[8 * j + 2 * e + 1]);
               }
             }
           }
@@ -1165,27 +1235,37 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
 
   int tile = tile_from_force(force_bm, force_bn);
   if (tile < 0) {
-    // Makespan model for the dynamic (cluster-launch-control) schedule: every CTA computes
-    // 128 rows x BN columns per tile, so its time per tile ~ BN * (K + fixed per-tile cost);
-    // with T tiles over `slots` co-resident units the last one finishes after about
-    // T / slots + 1/2 tiles (one tile when T <= slots). Per-flop factors measured on B200:
-    // the 256x512 pair tile moves 25% fewer operand bytes per flop, which keeps clocks
-    // higher under the power cap; narrower tiles leave the single UMMA-issuing thread less
-    // slack per k-block; one-CTA tiles read twice the B bytes per flop of a pair.
+    // Makespan model (cycles per CTA) for the dynamic cluster-launch-control schedule,
+    // calibrated on B200:
+    //   k-block time = max(UMMA time, issuer overhead). Every CTA owns 128 rows, so its UMMAs
+    //     take BN/2 cycles per k16 (4 per 64-k block); one thread also waits for the stage,
+    //     fences and commits, ~320 cycles per k-block whatever N is. An N=64 UMMA cannot be
+    //     issued faster than ~48 cycles (it executes in 32), so narrow tiles are
+    //     overhead-bound.
+    //   tile time = k-blocks x k-block time + hand-off / epilogue cost (double-buffered
+    //     accumulators hide most of it; the single 512-column accumulator does not).
+    //   makespan = one tile when the tiles fit the co-resident slots, else
+    //     tiles / slots + 1/2 tile of tail.
+    // Per-flop factors: the 256x512 pair tile moves 25% fewer operand bytes per flop, which
+    // keeps the clock higher under the 1 kW cap; one-CTA tiles read twice the B bytes.
     struct Cand {
       int tile;
-      double factor;
+      double factor, tile_cost;
     };
-    const Cand cands[] = {{kT256x512, 0.95}, {kT256x256, 1.00}, {kT256x128, 1.06},
-                          {kT128x256, 1.10}, {kT128x128, 1.15}, {kT128x64, 1.22}};
+    const Cand cands[] = {{kT256x512, 0.95, 4000.0}, {kT256x256, 1.00, 1500.0},
+                          {kT256x128, 1.00, 1500.0}, {kT128x256, 1.05, 1500.0},
+                          {kT128x128, 1.05, 1500.0}};
+    const double kb = std::ceil(static_cast<double>(K) / BK);
     double best = -1.0;
     for (const Cand &c : cands) {
       const TileInfo &ti = kTiles[c.tile];
       const double tiles =
           static_cast<double>(ceil_div(M, CTA_M * ti.pair)) * ceil_div(N, ti.bn);
       const double slots = ti.pair == 2 ? pair_slots : sm_count;
+      const double kb_time = std::max(4.0 * ti.bn / 2.0, 320.0);
+      const double tile_time = kb * kb_time + c.tile_cost;
       const double makespan = tiles <= slots ? 1.0 : tiles / slots + 0.5;
-      const double cost = makespan * ti.bn * (static_cast<double>(K) + 512.0) * c.factor;
+      const double cost = makespan * tile_time * c.factor;
       if (best < 0 || cost < best) {
         best = cost;
         tile = c.tile;
@@ -1202,8 +1282,14 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   const long long total = static_cast<long long>(pl->tiles_m) * pl->tiles_n;
   const int slots = ti.pair == 2 ? pair_slots : sm_count;
   const int units = static_cast<int>(std::min<long long>(total, slots));
-  // One cluster per tile; the running ones take over the rest (cluster launch control).
-  pl->grid_ctas = static_cast<int>(total * ti.pair);
+  // Schedule. Cluster launch control (one cluster per tile; the running ones take over the
+  // rest) balances long tiles across SMs that do not run at one clock, but one take-over
+  // round trip costs ~3-4.5 K cycles, so tiles shorter than that (small K), and grids whose
+  // tiles all fit at once, use a static persistent schedule instead.
+  const double tile_cycles =
+      std::ceil(static_cast<double>(K) / BK) * std::max(2.0 * ti.bn, 320.0);
+  pl->sched_static = (total <= slots || tile_cycles < kStaticTileCycles) ? 1 : 0;
+  pl->grid_ctas = static_cast<int>((pl->sched_static ? units : total) * ti.pair);
   if (group_m == 0) {
     // Working set of one wave ~ g tile-rows of A plus (units/g) tile-columns of B; choose g
     // near sqrt(units * tile_n / tile_m) (equal A and B footprints), at least 1.
@@ -1284,6 +1370,7 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   kp.beta = beta;
   kp.C = C;
   kp.timeout_ns = g_timeout_ns.load();
+  kp.sched_static = pl.sched_static;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid_ctas, 1, 1);

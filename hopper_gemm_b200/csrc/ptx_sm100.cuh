@@ -1,10 +1,10 @@
-// Inline-PTX primitives for the sm_100a GEMM: mbarriers, TMA (tiled, no multicast),
+// Inline-PTX primitives for the sm_100a GEMM: mbarriers, TMA (tiled, one destination CTA),
 // tcgen05 (TMEM allocation, UMMA issue, commit, TMEM loads) and bounded waits.
 //
 // These replace the sm_90a wrapper layer of the reference (mma_half.cu:247-435: mbarrier,
-// TMA load/store/multicast, setmaxnreg, wgmma fence/commit/wait). Nothing here issues a
-// TMA load with cluster multicast: the 2-SM UMMA pair shares operands through the
-// tensor core itself, and each CTA loads its own slice.
+// TMA load/store, cluster-broadcast loads, setmaxnreg, wgmma fence/commit/wait). Every TMA
+// load here writes only the issuing CTA's shared memory: the 2-SM UMMA pair shares operands
+// through the tensor core itself, and each CTA loads its own slice.
 #pragma once
 
 #include <cuda.h>
@@ -189,6 +189,13 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap *m, uint32_t 
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1)
       : "memory");
+}
+// Asks the TMA unit to bring a 2-D box into L2 (no shared memory, no completion signal).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *m, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *m, uint32_t src, int32_t c0,
                                              int32_t c1) {

@@ -122,12 +122,15 @@ typedef struct {
   int group_m;    /* raster band: > 0 tile rows (M fastest), < 0 tile columns (N fastest) */
   int stages;     /* smem pipeline depth */
   int tiles_m, tiles_n;
-  int grid_ctas;  /* CTAs launched: one cluster of `pair` CTAs per tile; running clusters
-                     take over not-yet-started ones (cluster launch control) */
+  int grid_ctas;  /* CTAs launched: with sched_static == 0 one cluster of `pair` CTAs per
+                     tile, running clusters taking over not-yet-started ones (cluster launch
+                     control); with sched_static == 1 one persistent cluster per slot */
   int pad_a, pad_b;      /* operand restrided into scratch (K % 8, N % 8) */
   int lda, ldb;          /* leading dimensions the tensor maps use */
   int tma_store;         /* 1: TMA-store epilogue (N % 8 == 0), 0: SIMT stores */
   size_t scratch_bytes;  /* scratch needed for restrided operands */
+  int sched_static;      /* 1: cluster c takes tiles c, c + clusters, ... (short tiles, or all
+                            tiles co-resident); 0: cluster launch control */
 } hgemm_plan_t;
 
 /* `aligned16` says whether A, B and C all start on 16-byte boundaries; `sm_count` and

@@ -68,3 +68,18 @@ def test_grid_is_one_cluster_per_tile():
     for M, N, K in [(16384, 16384, 16384), (384, 2048, 2048), (1, 4096, 4096), (8192, 8, 8192)]:
         p = hg.plan(M, N, K, **B200)
         assert p["grid_ctas"] == p["tiles_m"] * p["tiles_n"] * p["pair"]
+
+
+def test_schedule_choice():
+    # long tiles: one cluster per tile, the running clusters take over the rest
+    p = hg.plan(8192, 8192, 8192, **B200)
+    assert p["sched_static"] == 0
+    # short tiles (K = 128): persistent clusters, one per slot, static tile order
+    p = hg.plan(4096, 8192, 128, **B200)
+    assert p["sched_static"] == 1
+    slots = B200["pair_slots"] if p["pair"] == 2 else B200["sm_count"]
+    assert p["grid_ctas"] == min(p["tiles_m"] * p["tiles_n"], slots) * p["pair"]
+    # every tile co-resident: static, one cluster per tile
+    p = hg.plan(1024, 1024, 1024, **B200)
+    assert p["sched_static"] == 1
+    assert p["grid_ctas"] == p["tiles_m"] * p["tiles_n"] * p["pair"]
