@@ -1,14 +1,19 @@
 """Benchmark of the B200 FP16 GEMM (the path behind the reference's `solve`).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--M 8192 --N 8192 --K 8192] [--chunks C]
+                    [--M 8192 --N 8192 --K 8192] [--chunks C] [--workload gemm8192|sharded32k]
 
 Workload: FP16 GEMM C = A @ B (alpha=1, beta=0), row-major, A/B full-entropy U[-1,1) from the
 reference benchmark's counter-hash fill (three_way.cu:22-33, seeds three_way.cu:71-72).
-One step = one GEMM launch. At N=1 the shape is 8192^3, the configuration the metric is quoted
-on. With N GPUs (torchrun, one process per GPU) the job is the row-sharded GEMM of
-BASELINE configs[4]'s scheme at fixed per-GPU work: M = 8192*N rows split by rank, B
-replicated, and the C row blocks all-gathered over NCCL inside every step (weak scaling).
+One step = one GEMM (plus, with N GPUs, the all-gather of C). At N=1 the shape is 8192^3, the
+configuration the metric is quoted on. With N GPUs (torchrun, one process per GPU) the
+default job keeps the per-GPU work fixed (weak scaling): M = 8192*N rows split by rank, B
+replicated, and every rank ends each step with the whole C: one kernel per rank computes its
+rows and its epilogue TMA-stores each finished tile into every rank's C over NVLink (peer
+buffers mapped with CUDA IPC), followed by a 4-byte NCCL barrier (`--exchange nccl`: the GEMM
+then an NCCL all-gather instead). `--workload sharded32k`
+runs BASELINE configs[4] instead: the 32768x32768x16384 GEMM split by rows over the N GPUs
+(strong scaling).
 
 Timing follows the reference methodology (three_way.cu): L2 flushed (memset of 3x the L2
 size) before every timed launch, one launch between two CUDA events on the launching stream,
@@ -30,6 +35,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 FALLBACK_PEAK_TFLOPS = 1590.0
+DEFAULT_CHUNKS = 1  # --exchange nccl: measured fastest on 2 B200s (one in-place all-gather)
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -42,7 +48,16 @@ def parse():
     ap.add_argument("--M", type=int, default=8192, help="rows per GPU")
     ap.add_argument("--N", type=int, default=8192)
     ap.add_argument("--K", type=int, default=8192)
-    ap.add_argument("--chunks", type=int, default=1, help="row chunks for gather overlap (N>1)")
+    ap.add_argument("--chunks", type=int, default=0,
+                    help="row chunks per rank for gather overlap (N>1; 0 = automatic)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N>1: peer = one kernel per rank stores its tiles into every rank's C "
+                         "over NVLink (CUDA IPC); nccl = GEMM then NCCL all-gather / send-recv")
+    ap.add_argument("--reserved-sms", type=int, default=-1,
+                    help="SMs the chunk GEMMs leave to the exchange (N>1; -1 = library default)")
+    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "sharded32k"],
+                    help="gemm8192: 8192 rows x 8192 x 8192 per GPU (weak scaling); sharded32k: "
+                         "the 32768x32768x16384 GEMM split by rows over the GPUs (strong)")
     ap.add_argument("--force-bm", type=int, default=0, help="tile rows (0 = automatic)")
     ap.add_argument("--force-bn", type=int, default=0, help="tile columns (0 = automatic)")
     ap.add_argument("--group-m", type=int, default=0, help="raster band height (0 = automatic)")
@@ -346,8 +361,17 @@ def main():
         dist.init_process_group("nccl", device_id=dev,
                                 timeout=__import__("datetime").timedelta(seconds=120))
 
-    Ml, N, K = args.M, args.N, args.K
-    M = Ml * world
+    if args.workload == "sharded32k":
+        # A 32768x16384 split by rows, B 16384x32768 replicated.
+        M, N, K = 32768, 32768, 16384
+        if M % world:
+            raise SystemExit("sharded32k needs a GPU count that divides 32768")
+        Ml = M // world
+    else:
+        Ml, N, K = args.M, args.N, args.K
+        M = Ml * world
+    if args.chunks <= 0:
+        args.chunks = 1 if world == 1 else DEFAULT_CHUNKS
     flops_job = 2.0 * M * N * K
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
@@ -374,6 +398,14 @@ def main():
         st = hg.lib.hgemm_comm_init(ctypes.byref(comm_p), world, id_bytes, 128, rank)
         assert st == 0, hg.status_string(st)
         comm = comm_p
+        if args.reserved_sms >= 0:
+            st = hg.lib.hgemm_comm_set_reserved_sms(comm, args.reserved_sms)
+            assert st == 0, hg.status_string(st)
+        if args.exchange == "peer":
+            st = hg.lib.hgemm_comm_register_output(comm, C.data_ptr(),
+                                                   C.numel() * C.element_size())
+            if st != 0:
+                raise SystemExit(f"peer exchange unavailable: {hg.status_string(st)}")
 
     def ours():
         if comm is None:
@@ -487,22 +519,44 @@ def main():
                        "hgemm_sharded_rank() C ABI, pinned host buffers"}
         assert hg.last_status() == 0, hg.status_string(hg.last_status())
 
+    # The dominant kernel alone (roofline.achieved): at N=1 that is the timed launch itself;
+    # with N GPUs the step also holds the gather, so the local GEMM is timed separately here.
+    if world == 1:
+        kernel_ms = ms_ours
+    else:
+        def local_gemm():
+            st = hg.lib.hgemm_launch_ex(A.data_ptr(), B.data_ptr(), R.data_ptr(), Ml, N, K, 1.0,
+                                        0.0, sptr, args.force_bm, args.force_bn, args.group_m)
+            if st != 0:
+                raise RuntimeError(hg.status_string(st))
+        local_gemm()
+        kev = [sample(local_gemm) for _ in range(max(3, min(args.steps, 20)))]
+        torch.cuda.synchronize()
+        kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+
     st_dev, where = hg.device_status(clear=False)
     if comm is not None:
         hg.lib.hgemm_comm_destroy(comm)
 
     if rank == 0:
         peak, hbm, src = peaks()
-        achieved = 2.0 * Ml * N * K / (ms_ours * 1e-3) / 1e12 if world == 1 else \
-            2.0 * Ml * N * K / (statistics.mean(t_ours) * 1e-3) / 1e12
+        achieved = 2.0 * Ml * N * K / (kernel_ms * 1e-3) / 1e12
         traffic = profiled_traffic(Ml, N, K)
         line = {
             "metric": "fp16_gemm_tflops", "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_ours,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True,
+            "scaling": "strong" if args.workload == "sharded32k" else "weak",
+            "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (three_way.cu counter-hash fill, U[-1,1))",
             "config": {"workload": (f"gemm_{M}x{N}x{K}" if world == 1 else
-                                    f"gemm_{M}x{N}x{K}_rowsharded_allgather"),
+                                    f"gemm_{M}x{N}x{K}_rowsharded_" +
+                                    ("peerstore" if args.exchange == "peer" else "allgather")),
+                       "exchange": None if world == 1 else (
+                           "fused GEMM epilogue TMA-stores every tile to all ranks' C over "
+                           "NVLink (CUDA IPC peer mappings) + 4-byte NCCL barrier"
+                           if args.exchange == "peer" else
+                           f"NCCL all-gather / send-recv, {args.chunks} chunk(s)"),
                        "M": M, "N": N, "K": K, "alpha": 1.0, "beta": 0.0,
                        "rows_per_gpu": Ml, "parallelism": f"rowshard{world}",
                        "l2": "flushed (3x L2 memset) before every timed launch",
@@ -518,7 +572,8 @@ def main():
             "check_rel_l2_vs_cublas": spot_l2,
             "device_status": st_dev,
             "e2e": e2e,
-            "gpu_launches": args.steps * (1 if comm is None else max(1, args.chunks)),
+            "gpu_launches": args.steps * (1 if (comm is None or args.exchange == "peer")
+                                          else max(1, args.chunks)),
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:

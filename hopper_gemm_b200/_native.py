@@ -20,6 +20,7 @@ HGEMM_ERR_DEVICE_TIMEOUT = 6
 HGEMM_ERR_UNSUPPORTED_DEVICE = 7
 HGEMM_ERR_NCCL = 8
 HGEMM_ERR_TOO_LARGE = 9
+HGEMM_ERR_NOT_FUSABLE = 10
 
 
 class HgemmPlan(ctypes.Structure):
@@ -45,6 +46,8 @@ SIGNATURES = {
     "hgemm_launch": (_i, _GEMM + [_vp]),
     "hgemm_launch_ex": (_i, _GEMM + [_vp, _i, _i, _i]),
     "hgemm_launch_tuned": (_i, _GEMM + [_vp]),
+    "hgemm_launch_sm_limit": (_i, _GEMM + [_vp, _i]),
+    "hgemm_launch_peers": (_i, _GEMM + [_vp, _vp, _i, _i]),
     "hgemm_launch_noalloc": (_i, _GEMM + [_vp]),
     "hgemm_noalloc_scratch_bytes": (ctypes.c_size_t, []),
     "hgemm_last_status": (_i, []),
@@ -57,6 +60,8 @@ SIGNATURES = {
     "hgemm_comm_unique_id": (_i, [_vp, ctypes.c_size_t]),
     "hgemm_comm_init": (_i, [ctypes.POINTER(_vp), _i, _vp, ctypes.c_size_t, _i]),
     "hgemm_comm_destroy": (_i, [_vp]),
+    "hgemm_comm_set_reserved_sms": (_i, [_vp, _i]),
+    "hgemm_comm_register_output": (_i, [_vp, _vp, ctypes.c_size_t]),
     "hgemm_sharded_rank": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _f, _i, _vp]),
     "hgemm_shard_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "hgemm_shard_chunk_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),

@@ -9,6 +9,13 @@
 // With chunks > 1 the exchange of chunk c runs on a communication stream while the GEMM of
 // chunk c+1 runs on the caller's stream, so the NVLink transfer overlaps the math.
 //
+// Fused path: once every rank has registered its C buffer (hgemm_comm_register_output, which
+// maps the peers' buffers into this process through CUDA IPC), hgemm_sharded_rank runs ONE
+// kernel per rank whose epilogue TMA-stores every finished C tile into the local C and into
+// each peer's C over NVLink, tile by tile while the math goes on, followed by a 4-byte NCCL
+// all-reduce that serves as the barrier after which every rank's C is complete. No NCCL
+// kernel moves C data on this path.
+//
 // The reference (yz-wqf/Hopper_GEMM) is single-GPU and has no counterpart for this layer.
 // NCCL is resolved at run time from libnccl.so.2, so a process that already loaded NCCL
 // (e.g. through torch.distributed) shares that copy instead of pulling in a second one.
@@ -39,6 +46,8 @@ struct NcclApi {
   ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t,
                        cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                            ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
 };
@@ -59,15 +68,47 @@ const NcclApi &nccl() {
     HGEMM_SYM(AllGather, "ncclAllGather");
     HGEMM_SYM(Send, "ncclSend");
     HGEMM_SYM(Recv, "ncclRecv");
+    HGEMM_SYM(AllReduce, "ncclAllReduce");
     HGEMM_SYM(GroupStart, "ncclGroupStart");
     HGEMM_SYM(GroupEnd, "ncclGroupEnd");
 #undef HGEMM_SYM
     a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.CommAbort &&
-           a.CommGetAsyncError && a.AllGather && a.Send && a.Recv && a.GroupStart && a.GroupEnd;
+           a.CommGetAsyncError && a.AllGather && a.Send && a.Recv && a.AllReduce &&
+           a.GroupStart && a.GroupEnd;
     return a;
   }();
   return api;
 }
+
+constexpr int kDefaultReservedSms = 16;
+constexpr int kMaxRanks = 8;  // the fused path stores to at most 7 peers
+
+// Start and size of the allocation that contains `p` (driver entry point, no -lcuda).
+bool allocation_range(const void *p, char **base, size_t *size) {
+  using Fn = int (*)(unsigned long long *, size_t *, unsigned long long);
+  static Fn fn = [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      ptr = nullptr;
+    return reinterpret_cast<Fn>(ptr);
+  }();
+  unsigned long long b = 0;
+  if (!fn || fn(&b, size, reinterpret_cast<unsigned long long>(p)) != 0) return false;
+  *base = reinterpret_cast<char *>(b);
+  return true;
+}
+
+// What each rank publishes about its registered C buffer.
+struct OutputRecord {
+  cudaIpcMemHandle_t handle;
+  unsigned long long offset;  // C - allocation start
+  unsigned long long bytes;
+  int ok;
+  int pad;
+};
 
 }  // namespace
 
@@ -76,10 +117,39 @@ struct hgemm_comm_s {
   int nranks = 0;
   int rank = 0;
   int device = 0;
+  int sm_count = 0;
+  // SMs the chunk GEMMs leave free while chunks are exchanged, so that the collective's
+  // kernels run next to the GEMM instead of waiting for its persistent CTAs to exit.
+  int reserved_sms = kDefaultReservedSms;
   cudaStream_t comm_stream = nullptr;
   std::vector<cudaEvent_t> chunk_done;  // GEMM of chunk c finished (caller stream)
   cudaEvent_t gather_done = nullptr;     // all exchanges finished (comm stream)
+  // Fused path state.
+  int *barrier_word = nullptr;              // device int for the barrier all-reduce
+  OutputRecord *records_dev = nullptr;      // [nranks] gathered OutputRecords
+  hgemm_half_t *out_C = nullptr;            // this rank's registered C
+  size_t out_bytes = 0;
+  std::vector<void *> peer_base;            // [nranks] IPC mappings (nullptr for self)
+  std::vector<hgemm_half_t *> peer_C;       // [nranks] peers' registered C in this process
 };
+
+namespace {
+void unmap_outputs(hgemm_comm_s *c) {
+  for (void *b : c->peer_base)
+    if (b) cudaIpcCloseMemHandle(b);
+  c->peer_base.clear();
+  c->peer_C.clear();
+  c->out_C = nullptr;
+  c->out_bytes = 0;
+}
+void free_fused_state(hgemm_comm_s *c) {
+  unmap_outputs(c);
+  if (c->barrier_word) cudaFree(c->barrier_word);
+  if (c->records_dev) cudaFree(c->records_dev);
+  c->barrier_word = nullptr;
+  c->records_dev = nullptr;
+}
+}  // namespace
 
 extern "C" {
 
@@ -112,7 +182,9 @@ int hgemm_comm_init(hgemm_comm_t *out, int nranks, const void *id, size_t id_byt
   hgemm_comm_s *c = new hgemm_comm_s();
   c->nranks = nranks;
   c->rank = rank;
-  if (cudaGetDevice(&c->device) != cudaSuccess) {
+  if (cudaGetDevice(&c->device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, c->device) !=
+          cudaSuccess) {
     delete c;
     return HGEMM_ERR_CUDA;
   }
@@ -123,7 +195,11 @@ int hgemm_comm_init(hgemm_comm_t *out, int nranks, const void *id, size_t id_byt
     return HGEMM_ERR_NCCL;
   }
   if (cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaEventCreateWithFlags(&c->gather_done, cudaEventDisableTiming) != cudaSuccess) {
+      cudaEventCreateWithFlags(&c->gather_done, cudaEventDisableTiming) != cudaSuccess ||
+      cudaMalloc(&c->barrier_word, sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&c->records_dev, sizeof(OutputRecord) * nranks) != cudaSuccess ||
+      cudaMemset(c->barrier_word, 0, sizeof(int)) != cudaSuccess) {
+    free_fused_state(c);
     a.CommDestroy(c->comm);
     delete c;
     return HGEMM_ERR_CUDA;
@@ -138,6 +214,7 @@ int hgemm_comm_destroy(hgemm_comm_t c) {
   int st = HGEMM_OK;
   if (c->comm_stream) cudaStreamSynchronize(c->comm_stream);
   if (c->comm && a.ok && a.CommDestroy(c->comm) != ncclSuccess) st = HGEMM_ERR_NCCL;
+  free_fused_state(c);
   for (cudaEvent_t e : c->chunk_done) cudaEventDestroy(e);
   if (c->gather_done) cudaEventDestroy(c->gather_done);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
@@ -160,6 +237,7 @@ int hgemm_comm_abort(hgemm_comm_t c) {
   int st = HGEMM_OK;
   if (c->comm && a.ok && a.CommAbort(c->comm) != ncclSuccess) st = HGEMM_ERR_NCCL;
   c->comm = nullptr;
+  free_fused_state(c);
   for (cudaEvent_t e : c->chunk_done) cudaEventDestroy(e);
   if (c->gather_done) cudaEventDestroy(c->gather_done);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
@@ -172,6 +250,73 @@ int hgemm_shard_chunk_rows(int rows, int chunks, int chunk, int *begin, int *cou
     return HGEMM_ERR_INVALID_ARG;
   *begin = static_cast<int>(static_cast<long long>(rows) * chunk / chunks);
   *count = static_cast<int>(static_cast<long long>(rows) * (chunk + 1) / chunks) - *begin;
+  return HGEMM_OK;
+}
+
+int hgemm_comm_register_output(hgemm_comm_t c, hgemm_half_t *C, size_t bytes) {
+  if (!c || (C == nullptr) != (bytes == 0)) return HGEMM_ERR_INVALID_ARG;
+  const NcclApi &a = nccl();
+  if (!a.ok || !c->comm) return HGEMM_ERR_NCCL;
+  const int P = c->nranks, me = c->rank;
+  if (cudaStreamSynchronize(c->comm_stream) != cudaSuccess) return HGEMM_ERR_CUDA;
+  unmap_outputs(c);
+  // Every rank takes part in both collectives below, whatever happened locally, so that the
+  // ranks stay in step; the outcome is agreed on with a MIN all-reduce.
+  OutputRecord mine;
+  std::memset(&mine, 0, sizeof(mine));
+  char *base = nullptr;
+  size_t size = 0;
+  if (C && P <= kMaxRanks && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
+      allocation_range(C, &base, &size) && cudaIpcGetMemHandle(&mine.handle, base) == cudaSuccess) {
+    mine.offset = static_cast<unsigned long long>(reinterpret_cast<char *>(C) - base);
+    mine.bytes = bytes;
+    mine.ok = (mine.offset + bytes <= size) ? 1 : 0;
+  }
+  cudaGetLastError();
+  std::vector<OutputRecord> all(P);
+  bool ok = cudaMemcpy(c->records_dev + me, &mine, sizeof(mine), cudaMemcpyHostToDevice) ==
+                cudaSuccess &&
+            a.AllGather(c->records_dev + me, c->records_dev, sizeof(OutputRecord), ncclUint8,
+                        c->comm, c->comm_stream) == ncclSuccess &&
+            cudaStreamSynchronize(c->comm_stream) == cudaSuccess &&
+            cudaMemcpy(all.data(), c->records_dev, sizeof(OutputRecord) * P,
+                       cudaMemcpyDeviceToHost) == cudaSuccess;
+  int local_ok = ok ? 1 : 0;
+  c->peer_base.assign(P, nullptr);
+  c->peer_C.assign(P, nullptr);
+  for (int r = 0; r < P && local_ok; ++r) {
+    if (!all[r].ok || all[r].bytes != bytes) local_ok = 0;
+    if (r == me || !local_ok) continue;
+    void *pb = nullptr;
+    if (cudaIpcOpenMemHandle(&pb, all[r].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      local_ok = 0;
+      break;
+    }
+    c->peer_base[r] = pb;
+    c->peer_C[r] = reinterpret_cast<hgemm_half_t *>(static_cast<char *>(pb) + all[r].offset);
+  }
+  if (!C) local_ok = 0;
+  int agreed = 0;
+  ok = cudaMemcpy(c->barrier_word, &local_ok, sizeof(int), cudaMemcpyHostToDevice) ==
+           cudaSuccess &&
+       a.AllReduce(c->barrier_word, c->barrier_word, 1, ncclInt32, ncclMin, c->comm,
+                   c->comm_stream) == ncclSuccess &&
+       cudaStreamSynchronize(c->comm_stream) == cudaSuccess &&
+       cudaMemcpy(&agreed, c->barrier_word, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess;
+  if (!ok || !agreed) {
+    unmap_outputs(c);
+    if (!ok) return HGEMM_ERR_NCCL;
+    return C ? HGEMM_ERR_CUDA : HGEMM_OK;
+  }
+  c->out_C = C;
+  c->out_bytes = bytes;
+  return HGEMM_OK;
+}
+
+int hgemm_comm_set_reserved_sms(hgemm_comm_t c, int sms) {
+  if (!c || sms < 0 || sms >= c->sm_count) return HGEMM_ERR_INVALID_ARG;
+  c->reserved_sms = sms;
   return HGEMM_OK;
 }
 
@@ -196,6 +341,34 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
     hgemm_shard_chunk_rows(count, chunks, ch, cb, cn);
   };
 
+  if (c->out_C && C == c->out_C && M % P == 0 && P > 1 &&
+      static_cast<size_t>(M) * N * sizeof(hgemm_half_t) <= c->out_bytes) {
+    // Fused path: one kernel computes this rank's rows and stores each tile into every
+    // peer's C as well; the barrier all-reduce follows whatever happened locally, so that
+    // the ranks' collective sequences stay the same.
+    hgemm_half_t *peers[kMaxRanks];
+    int n = 0;
+    for (int r = 0; r < P; ++r)
+      if (r != me) peers[n++] = c->peer_C[r] + static_cast<size_t>(rb) * row_elems;
+    hgemm_half_t *Cl = C + static_cast<size_t>(rb) * row_elems;
+    int st = HGEMM_OK;
+    if (rc > 0) {
+      st = hgemm_launch_peers(A_local, B, Cl, rc, N, K, alpha, beta, stream, peers, n, 0);
+      if (st == HGEMM_ERR_NOT_FUSABLE) {
+        // Shapes without TMA stores: compute locally, then push the rows with copies.
+        st = hgemm_launch_ex(A_local, B, Cl, rc, N, K, alpha, beta, stream, 0, 0, 0);
+        for (int i = 0; i < n && st == HGEMM_OK; ++i)
+          if (cudaMemcpyAsync(peers[i], Cl, static_cast<size_t>(rc) * row_elems * 2,
+                              cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+            st = HGEMM_ERR_CUDA;
+      }
+    }
+    if (a.AllReduce(c->barrier_word, c->barrier_word, 1, ncclInt32, ncclMax, c->comm, s) !=
+        ncclSuccess)
+      return HGEMM_ERR_NCCL;
+    return st;
+  }
+
   if (M % P == 0 && chunks == 1) {
     int st = HGEMM_OK;
     if (rc > 0)
@@ -218,9 +391,12 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
     int cb = 0, cn = 0;
     chunk_rows(rc, ch, &cb, &cn);
     if (cn > 0) {
-      const int st = hgemm_launch_ex(A_local + static_cast<size_t>(cb) * K, B,
-                                     C + static_cast<size_t>(rb + cb) * row_elems, cn, N, K,
-                                     alpha, beta, stream, 0, 0, 0);
+      const hgemm_half_t *Ac = A_local + static_cast<size_t>(cb) * K;
+      hgemm_half_t *Cc = C + static_cast<size_t>(rb + cb) * row_elems;
+      const int limit = c->sm_count - c->reserved_sms;
+      const int st = (P > 1 && c->reserved_sms > 0 && limit > 0)
+                         ? hgemm_launch_sm_limit(Ac, B, Cc, cn, N, K, alpha, beta, stream, limit)
+                         : hgemm_launch_ex(Ac, B, Cc, cn, N, K, alpha, beta, stream, 0, 0, 0);
       if (st != HGEMM_OK) return st;
     }
     if (P == 1) continue;

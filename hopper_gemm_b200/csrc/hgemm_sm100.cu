@@ -58,6 +58,8 @@ constexpr int EPI_COLS = 64;    // columns per epilogue chunk (one 128-byte swiz
 constexpr int NUM_THREADS = 192;
 constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in dynamic shared memory per block
 constexpr int BAR_BYTES = 512;
+// Peer-store launches keep the 256x512 tile only from this K on (longer main loop per tile).
+constexpr int kPeerWideTileMinK = 12288;
 // Tiles whose main loop is estimated shorter than this (cycles) use the static schedule.
 constexpr double kStaticTileCycles = 8192.0;
 
@@ -111,6 +113,15 @@ struct KParams {
   __half *C;
   unsigned long long timeout_ns;
   int sched_static;  // 1: cluster c takes tiles c, c + clusters, ...; 0: cluster launch control
+};
+
+// Other destinations of every C tile (e.g. the C buffers of peer GPUs mapped into this
+// process): the epilogue issues the same TMA store once more per map, so a row-sharded GEMM
+// delivers its rows to every rank while it computes them.
+constexpr int kMaxPeers = 7;
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];
+  int n;
 };
 
 // ============================================================================ device helpers
@@ -196,7 +207,8 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int j) {
 template <int PAIR, int BN, bool TMA_EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     hgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const KParams p) {
+                    const __grid_constant__ CUtensorMap tmC, const KParams p,
+                    const __grid_constant__ PeerMaps peers) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
   using Cfg = TileCfg<PAIR, BN>;
   constexpr int S = Cfg::STAGES;
@@ -254,7 +266,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmB);
-    if (TMA_EPI) ptx::prefetch_tmap(&tmC);
+    if (TMA_EPI) {
+      ptx::prefetch_tmap(&tmC);
+      for (int d = 0; d < peers.n; ++d) ptx::prefetch_tmap(&peers.m[d]);
+    }
   }
   if (warp == 1) {
     ptx::tmem_alloc<PAIR>(ptx::smem_u32(tmem_holder), Cfg::TMEM_COLS);
@@ -767,8 +782,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               __syncwarp();
               if (lane == 0) {
                 const int ccol = col0 + h * (BN / 2) + ch * EPI_COLS;
-                if (row0 < p.M && ccol < p.N)
+                if (row0 < p.M && ccol < p.N) {
                   ptx::tma_store_2d(&tmC, ptx::smem_u32(stg0) + buf, ccol, row0);
+                  for (int d = 0; d < peers.n; ++d)
+                    ptx::tma_store_2d(&peers.m[d], ptx::smem_u32(stg0) + buf, ccol, row0);
+                }
                 ptx::bulk_commit_group();
               }
             }
@@ -882,7 +900,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (row0 < p.M && ccol < p.N) ptx::tma_store_2d(&tmC, ptx::smem_u32(stg), ccol, row0);
+            if (row0 < p.M && ccol < p.N) {
+              ptx::tma_store_2d(&tmC, ptx::smem_u32(stg), ccol, row0);
+              for (int d = 0; d < peers.n; ++d)
+                ptx::tma_store_2d(&peers.m[d], ptx::smem_u32(stg), ccol, row0);
+            }
             ptx::bulk_commit_group();  // one group per chunk, empty when nothing was stored
           }
         } else {
@@ -943,7 +965,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (aborted_chunks) break;
       ++it;
     }
-    if (TMA_EPI && lane == 0) ptx::bulk_wait_group<0>();
+    if (TMA_EPI && lane == 0) {
+      ptx::bulk_wait_group<0>();
+      // Stores into peers' memory: complete and ordered system-wide before the CTA exits.
+      if (peers.n > 0) __threadfence_system();
+    }
     __syncwarp();
   }
 
@@ -1116,7 +1142,7 @@ constexpr TileInfo kTiles[kNumTiles] = {
     {1, 64, TileCfg<1, 64>::STAGES, TileCfg<1, 64>::SMEM, TileCfg<1, 64>::ACC_BUFS},
 };
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, KParams);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, KParams, PeerMaps);
 
 KernelFn kernel_for(int tile, bool tma_epi) {
   switch (tile) {
@@ -1201,7 +1227,8 @@ int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b
 // flop is the lowest. group_m keeps the concurrently running tiles' A and B blocks small
 // enough to stay in the 126 MB L2.
 int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int force_bn,
-              int group_m, int sm_count, int pair_slots, hgemm_plan_t *pl) {
+              int group_m, int sm_count, int pair_slots, hgemm_plan_t *pl,
+              bool persistent_only = false) {
   std::memset(pl, 0, sizeof(*pl));
   if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
   if ((force_bm != 0 || force_bn != 0) && tile_from_force(force_bm, force_bn) < 0)
@@ -1288,7 +1315,10 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   // tiles all fit at once, use a static persistent schedule instead.
   const double tile_cycles =
       std::ceil(static_cast<double>(K) / BK) * std::max(2.0 * ti.bn, 320.0);
-  pl->sched_static = (total <= slots || tile_cycles < kStaticTileCycles) ? 1 : 0;
+  // persistent_only: the GEMM must stay on `sm_count` SMs (the others run concurrent work),
+  // which only the static schedule guarantees.
+  pl->sched_static =
+      (persistent_only || total <= slots || tile_cycles < kStaticTileCycles) ? 1 : 0;
   pl->grid_ctas = static_cast<int>((pl->sched_static ? units : total) * ti.pair);
   if (group_m == 0) {
     // Working set of one wave ~ g tile-rows of A plus (units/g) tile-columns of B; choose g
@@ -1337,7 +1367,8 @@ int launch_simt(const __half *A, const __half *B, __half *C, int M, int N, int K
 // Launch the tcgen05 kernel for an already-made plan on operands with 16-byte strides.
 int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const __half *B,
               int ldb, __half *C, int M, int N, int K, float alpha, float beta,
-              cudaStream_t stream, DevState &d) {
+              cudaStream_t stream, DevState &d, __half *const *peer_C = nullptr,
+              int npeers = 0) {
   const TileInfo &ti = kTiles[tile];
   const bool tma_epi = pl.tma_store != 0;
   CUtensorMap ta, tb, tc;
@@ -1347,6 +1378,18 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
     if (!encode_2d(&tc, C, M, N, N, EPI_ROWS, EPI_COLS)) return HGEMM_ERR_TENSOR_MAP;
   } else {
     tc = ta;
+  }
+  PeerMaps peers;
+  std::memset(&peers, 0, sizeof(peers));
+  if (npeers > 0) {
+    if (!tma_epi || npeers > kMaxPeers || !peer_C) return HGEMM_ERR_NOT_FUSABLE;
+    for (int i = 0; i < npeers; ++i) {
+      if (!peer_C[i] || reinterpret_cast<uintptr_t>(peer_C[i]) % 16 != 0)
+        return HGEMM_ERR_NOT_FUSABLE;
+      if (!encode_2d(&peers.m[i], peer_C[i], M, N, N, EPI_ROWS, EPI_COLS))
+        return HGEMM_ERR_TENSOR_MAP;
+    }
+    peers.n = npeers;
   }
   KernelFn k = kernel_for(tile, tma_epi);
   if (!d.attr_done[tile][tma_epi]) {
@@ -1384,7 +1427,7 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = ti.pair == 2 ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, k, ta, tb, tc, kp) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, k, ta, tb, tc, kp, peers) != cudaSuccess) {
     cudaGetLastError();
     return HGEMM_ERR_LAUNCH;
   }
@@ -1392,7 +1435,8 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
 }
 
 int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K, float alpha,
-                float beta, cudaStream_t stream, int force_bm, int force_bn, int group_m) {
+                float beta, cudaStream_t stream, int force_bm, int force_bn, int group_m,
+                int sm_limit = 0, __half *const *peer_C = nullptr, int npeers = 0) {
   if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return HGEMM_OK;
   if (!A || !B || !C) return HGEMM_ERR_INVALID_ARG;
@@ -1405,11 +1449,25 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
   const bool aligned16 = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+  int sms = d->sm_count, pslots = d->pair_slots;
+  if (sm_limit > 0 && sm_limit < sms) {
+    sms = sm_limit;
+    pslots = std::max(1, std::min(pslots, sm_limit / 2));
+  }
   hgemm_plan_t pl;
-  st = make_plan(M, N, K, beta, aligned16, force_bm, force_bn, group_m, d->sm_count,
-                 d->pair_slots, &pl);
+  st = make_plan(M, N, K, beta, aligned16, force_bm, force_bn, group_m, sms, pslots, &pl,
+                 sm_limit > 0);
   if (st != HGEMM_OK) return st;
   if (pl.path == 0) return HGEMM_OK;
+  if (npeers > 0 && (pl.path != 1 || !pl.tma_store)) return HGEMM_ERR_NOT_FUSABLE;
+  if (npeers > 0 && force_bm == 0 && pl.tile_n == 512 && K < kPeerWideTileMinK) {
+    // Every tile's epilogue also stores to the peers. With the single 512-column
+    // accumulator that longer epilogue sits between tiles; the double-buffered 256x256 tile
+    // hides it behind the next tile's main loop (measured on 2 B200s: faster at K = 8192,
+    // slower at K = 16384).
+    st = make_plan(M, N, K, beta, aligned16, 256, 256, group_m, sms, pslots, &pl, sm_limit > 0);
+    if (st != HGEMM_OK) return st;
+  }
   if (pl.path == 2) return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
 
   const __half *Ause = A, *Buse = B;
@@ -1431,7 +1489,8 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
   int tile = -1;
   for (int t = 0; t < kNumTiles; ++t)
     if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;
-  return launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, C, M, N, K, alpha, beta, stream, *d);
+  return launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, C, M, N, K, alpha, beta, stream, *d,
+                   peer_C, npeers);
 }
 
 // ---------------------------------------------------------------- autotune cache
@@ -1454,6 +1513,24 @@ int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *
   return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
                                 reinterpret_cast<cudaStream_t>(stream), force_bm, force_bn,
                                 group_m));
+}
+
+int hgemm_launch_peers(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                       int N, int K, float alpha, float beta, hgemm_stream_t stream,
+                       hgemm_half_t *const *peer_C, int npeers, int sm_limit) {
+  if (npeers < 0 || npeers > kMaxPeers || (npeers > 0 && !peer_C))
+    return set_status(HGEMM_ERR_INVALID_ARG);
+  return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
+                                reinterpret_cast<cudaStream_t>(stream), 0, 0, 0,
+                                sm_limit > 0 ? sm_limit : 0, peer_C, npeers));
+}
+
+int hgemm_launch_sm_limit(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                          int N, int K, float alpha, float beta, hgemm_stream_t stream,
+                          int sm_limit) {
+  if (sm_limit <= 0) return set_status(HGEMM_ERR_INVALID_ARG);
+  return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
+                                reinterpret_cast<cudaStream_t>(stream), 0, 0, 0, sm_limit));
 }
 
 int hgemm_launch(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N,
@@ -1553,6 +1630,7 @@ const char *hgemm_status_string(int s) {
     case HGEMM_ERR_UNSUPPORTED_DEVICE: return "device is not sm_100 (B200)";
     case HGEMM_ERR_NCCL: return "NCCL unavailable or failed";
     case HGEMM_ERR_TOO_LARGE: return "size beyond this entry point's limit";
+    case HGEMM_ERR_NOT_FUSABLE: return "shape or alignment takes a path without TMA stores";
     default: return "unknown status";
   }
 }

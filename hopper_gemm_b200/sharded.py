@@ -6,6 +6,11 @@ every rank ends with the whole C (hgemm_sharded_rank in libhgemm_b200.so: one in
 ncclAllGather for equal blocks, grouped send/recv otherwise or when the local rows are split
 into chunks whose exchange overlaps the next chunk's GEMM).
 
+register_output(C) switches a communicator to the fused path for that output buffer: the
+peers' C buffers are mapped into every process (CUDA IPC) and a single kernel per rank stores
+each finished tile into every rank's C over NVLink while it computes, so the exchange
+overlaps the math tile by tile; a 4-byte NCCL all-reduce is the only collective per call.
+
 torch.distributed (any backend) is used only for the rendezvous: rank 0 creates the NCCL id
 and broadcasts it; the library then owns its own NCCL communicator. The reference
 (yz-wqf/Hopper_GEMM) is single-GPU; this layer has no counterpart there.
@@ -64,6 +69,21 @@ class RowShardedGemm:
         if st != HGEMM_OK:
             raise HgemmError(st, "hgemm_sharded_rank")
         return C
+
+    def register_output(self, C):
+        """Collective: use the fused peer-store path whenever C (this rank's full M x N output
+        buffer, the same tensor on every later call) is passed. Returns False when some rank
+        could not map its buffer (the NCCL path stays in use)."""
+        st = lib.hgemm_comm_register_output(self._comm, C.data_ptr(),
+                                            C.numel() * C.element_size())
+        if st not in (HGEMM_OK,):
+            return False
+        return True
+
+    def unregister_output(self):
+        st = lib.hgemm_comm_register_output(self._comm, None, 0)
+        if st != HGEMM_OK:
+            raise HgemmError(st, "hgemm_comm_register_output")
 
     def healthy(self):
         return lib.hgemm_comm_check(self._comm) == HGEMM_OK

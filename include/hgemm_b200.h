@@ -45,6 +45,8 @@ typedef struct CUstream_st *hgemm_stream_t;
 #define HGEMM_ERR_UNSUPPORTED_DEVICE 7 /* not a compute capability 10.0 device */
 #define HGEMM_ERR_NCCL 8             /* NCCL missing or an NCCL call failed */
 #define HGEMM_ERR_TOO_LARGE 9        /* size beyond what this entry point supports */
+#define HGEMM_ERR_NOT_FUSABLE 10     /* peer stores need the TMA-store tile path (N % 8 == 0,
+                                        16-byte aligned C, K > 0); nothing was launched */
 
 /* ---------------------------------------------------------------- GEMM entry points */
 
@@ -113,6 +115,24 @@ int hgemm_selftest_wait_timeout(unsigned long long timeout_ns);
 /* Frees the per-device scratch used to restride A (K % 8 != 0) or B (N % 8 != 0). */
 void hgemm_release(void);
 
+/* Like hgemm_launch, but the GEMM runs on at most `sm_limit` SMs (persistent CTAs with a
+ * static tile order), leaving the remaining SMs free for work that must run at the same time,
+ * such as the collective kernels of hgemm_sharded_rank. No counterpart in the reference. */
+int hgemm_launch_sm_limit(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                          int N, int K, float alpha, float beta, hgemm_stream_t stream,
+                          int sm_limit);
+
+/* Like hgemm_launch_sm_limit (sm_limit <= 0: every SM), and every C tile is also written
+ * into `npeers` (<= 7) other M x N row-major buffers, such as the C buffers of peer GPUs
+ * mapped into this process: the epilogue issues one more TMA store per destination. The
+ * peer buffers are written asynchronously from the kernel; the caller orders their readers
+ * after it (hgemm_sharded_rank does so with a collective barrier). Returns
+ * HGEMM_ERR_NOT_FUSABLE without launching when the shape takes a path without TMA stores.
+ * No counterpart in the reference. */
+int hgemm_launch_peers(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                       int N, int K, float alpha, float beta, hgemm_stream_t stream,
+                       hgemm_half_t *const *peer_C, int npeers, int sm_limit);
+
 /* Host-only description of what hgemm_launch_ex would run; needs no GPU. */
 typedef struct {
   int path;       /* 0 no-op, 1 tcgen05 tiles, 2 SIMT fallback */
@@ -149,6 +169,21 @@ typedef struct hgemm_comm_s *hgemm_comm_t;
 int hgemm_comm_unique_id(void *id_out, size_t id_bytes); /* id_bytes >= 128 */
 int hgemm_comm_init(hgemm_comm_t *comm, int nranks, const void *id, size_t id_bytes, int rank);
 int hgemm_comm_destroy(hgemm_comm_t comm);
+
+/* Collective (every rank calls it): registers this rank's full M x N output buffer C
+ * (`bytes` long, 16-byte aligned, from cudaMalloc) and maps every peer's registered buffer
+ * into this process through CUDA IPC. While registered, hgemm_sharded_rank called with that
+ * buffer (on every rank) and M % nranks == 0 runs the fused path: one kernel per rank that
+ * stores each finished tile into all ranks' C over NVLink, then a 4-byte barrier
+ * all-reduce; no NCCL kernel moves C. C == NULL, bytes == 0 unregisters. Returns HGEMM_OK
+ * only when every rank registered (the outcome is agreed on collectively). No counterpart
+ * in the reference. */
+int hgemm_comm_register_output(hgemm_comm_t comm, hgemm_half_t *C, size_t bytes);
+
+/* SMs that the chunk GEMMs of hgemm_sharded_rank (chunks > 1, nranks > 1) leave free for
+ * the exchange kernels that run next to them (default 16; 0 = the GEMM takes every SM).
+ * No counterpart in the reference. */
+int hgemm_comm_set_reserved_sms(hgemm_comm_t comm, int sms);
 
 /* A_local: this rank's rows of A (rows x K); B: full K x N on this device; C: full M x N on
  * this device (the local row block is read when beta != 0). Equal row blocks

@@ -33,7 +33,7 @@ def _inputs(M, N, K, seed=5):
     return g.uniform_half((M, K)), g.uniform_half((K, N)), g.normal_half((M, N))
 
 
-def _worker(rank, world, port, M, N, K, chunks, alpha, beta, out):
+def _worker(rank, world, port, M, N, K, chunks, alpha, beta, out, fused=False):
     import sys
     sys.path.insert(0, ROOT)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -51,6 +51,13 @@ def _worker(rank, world, port, M, N, K, chunks, alpha, beta, out):
     dB = torch.from_numpy(B).cuda()
     dC = torch.from_numpy(C).cuda()
     sg = RowShardedGemm(M, N, K, rank, world, chunks=chunks)
+    if fused:
+        # peer-store path: registration maps the other rank's C; two calls in a row
+        assert sg.register_output(dC)
+        sg(dA, dB, dC, alpha, beta)
+        torch.cuda.synchronize()
+        dC.copy_(torch.from_numpy(C).cuda())
+        dist.barrier()
     sg(dA, dB, dC, alpha, beta)
     torch.cuda.synchronize()
     assert sg.healthy()
@@ -94,6 +101,26 @@ def test_two_ranks_gather_full_c(cuda, M, chunks):
     out = ctx.Manager().dict()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, chunks, 1.0, 0.5, out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(out) == {0: True, 1: True}
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+@pytest.mark.parametrize("M,N", [(4096, 1024), (2048, 1002), (3001, 1024)])
+def test_two_ranks_fused_peer_stores(cuda, M, N):
+    # (4096, 1024): one kernel per rank stores every tile into both ranks' C;
+    # (2048, 1002): N % 8 != 0 has no TMA-store epilogue, rows are pushed with copies;
+    # (3001, 1024): unequal row blocks keep the NCCL exchange although C is registered.
+    world, K = 2, 768
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, 1, 1.5, 0.5, out, True))
              for r in range(world)]
     for p in procs:
         p.start()
