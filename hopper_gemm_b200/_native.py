@@ -55,6 +55,7 @@ SIGNATURES = {
     "hgemm_device_status": (_i, [_i, ctypes.POINTER(_i)]),
     "hgemm_set_wait_timeout_ns": (None, [ctypes.c_ulonglong]),
     "hgemm_selftest_wait_timeout": (_i, [ctypes.c_ulonglong]),
+    "hgemm_selftest_peer_barrier": (_i, [ctypes.c_ulonglong]),
     "hgemm_release": (None, []),
     "hgemm_plan": (_i, [_i, _i, _i, _f, _i, _i, _i, _i, _i, _i, ctypes.POINTER(HgemmPlan)]),
     "hgemm_comm_unique_id": (_i, [_vp, ctypes.c_size_t]),
@@ -62,6 +63,7 @@ SIGNATURES = {
     "hgemm_comm_destroy": (_i, [_vp]),
     "hgemm_comm_set_reserved_sms": (_i, [_vp, _i]),
     "hgemm_comm_register_output": (_i, [_vp, _vp, ctypes.c_size_t]),
+    "hgemm_comm_output_ptr": (_i, [_vp, _i, ctypes.POINTER(_vp)]),
     "hgemm_sharded_rank": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _f, _f, _i, _vp]),
     "hgemm_shard_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "hgemm_shard_chunk_rows": (_i, [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),

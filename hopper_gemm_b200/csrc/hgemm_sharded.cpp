@@ -12,9 +12,9 @@
 // Fused path: once every rank has registered its C buffer (hgemm_comm_register_output, which
 // maps the peers' buffers into this process through CUDA IPC), hgemm_sharded_rank runs ONE
 // kernel per rank whose epilogue TMA-stores every finished C tile into the local C and into
-// each peer's C over NVLink, tile by tile while the math goes on, followed by a 4-byte NCCL
-// all-reduce that serves as the barrier after which every rank's C is complete. No NCCL
-// kernel moves C data on this path.
+// each peer's C over NVLink, tile by tile while the math goes on, followed by a one-warp
+// barrier kernel that exchanges step epochs through flag arrays mapped the same way (release
+// stores / acquire loads at system scope, bounded waits). No NCCL call is made on this path.
 //
 // The reference (yz-wqf/Hopper_GEMM) is single-GPU and has no counterpart for this layer.
 // NCCL is resolved at run time from libnccl.so.2, so a process that already loaded NCCL
@@ -31,6 +31,11 @@
 #include <vector>
 
 #include "hgemm_b200.h"
+
+// Cross-GPU flag barrier (hgemm_sm100.cu; internal to this library).
+extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_peer_barrier(
+    unsigned long long *const *flags, int rank, int nranks, unsigned long long epoch,
+    hgemm_stream_t stream);
 
 namespace {
 
@@ -101,9 +106,10 @@ bool allocation_range(const void *p, char **base, size_t *size) {
   return true;
 }
 
-// What each rank publishes about its registered C buffer.
+// What each rank publishes about its registered C buffer and its barrier flags.
 struct OutputRecord {
   cudaIpcMemHandle_t handle;
+  cudaIpcMemHandle_t flags_handle;
   unsigned long long offset;  // C - allocation start
   unsigned long long bytes;
   int ok;
@@ -125,7 +131,11 @@ struct hgemm_comm_s {
   std::vector<cudaEvent_t> chunk_done;  // GEMM of chunk c finished (caller stream)
   cudaEvent_t gather_done = nullptr;     // all exchanges finished (comm stream)
   // Fused path state.
-  int *barrier_word = nullptr;              // device int for the barrier all-reduce
+  int *barrier_word = nullptr;              // device int for the registration all-reduce
+  unsigned long long *flags = nullptr;      // [kMaxRanks] step epochs announced by each rank
+  unsigned long long epoch = 0;             // fused steps issued by this rank
+  std::vector<void *> peer_flags_base;      // [nranks] IPC mappings of the peers' flags
+  std::vector<unsigned long long *> peer_flags;
   OutputRecord *records_dev = nullptr;      // [nranks] gathered OutputRecords
   hgemm_half_t *out_C = nullptr;            // this rank's registered C
   size_t out_bytes = 0;
@@ -137,8 +147,12 @@ namespace {
 void unmap_outputs(hgemm_comm_s *c) {
   for (void *b : c->peer_base)
     if (b) cudaIpcCloseMemHandle(b);
+  for (void *b : c->peer_flags_base)
+    if (b) cudaIpcCloseMemHandle(b);
   c->peer_base.clear();
   c->peer_C.clear();
+  c->peer_flags_base.clear();
+  c->peer_flags.clear();
   c->out_C = nullptr;
   c->out_bytes = 0;
 }
@@ -146,6 +160,8 @@ void free_fused_state(hgemm_comm_s *c) {
   unmap_outputs(c);
   if (c->barrier_word) cudaFree(c->barrier_word);
   if (c->records_dev) cudaFree(c->records_dev);
+  if (c->flags) cudaFree(c->flags);
+  c->flags = nullptr;
   c->barrier_word = nullptr;
   c->records_dev = nullptr;
 }
@@ -198,6 +214,8 @@ int hgemm_comm_init(hgemm_comm_t *out, int nranks, const void *id, size_t id_byt
       cudaEventCreateWithFlags(&c->gather_done, cudaEventDisableTiming) != cudaSuccess ||
       cudaMalloc(&c->barrier_word, sizeof(int)) != cudaSuccess ||
       cudaMalloc(&c->records_dev, sizeof(OutputRecord) * nranks) != cudaSuccess ||
+      cudaMalloc(&c->flags, sizeof(unsigned long long) * kMaxRanks) != cudaSuccess ||
+      cudaMemset(c->flags, 0, sizeof(unsigned long long) * kMaxRanks) != cudaSuccess ||
       cudaMemset(c->barrier_word, 0, sizeof(int)) != cudaSuccess) {
     free_fused_state(c);
     a.CommDestroy(c->comm);
@@ -267,7 +285,8 @@ int hgemm_comm_register_output(hgemm_comm_t c, hgemm_half_t *C, size_t bytes) {
   char *base = nullptr;
   size_t size = 0;
   if (C && P <= kMaxRanks && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
-      allocation_range(C, &base, &size) && cudaIpcGetMemHandle(&mine.handle, base) == cudaSuccess) {
+      allocation_range(C, &base, &size) && cudaIpcGetMemHandle(&mine.handle, base) == cudaSuccess &&
+      cudaIpcGetMemHandle(&mine.flags_handle, c->flags) == cudaSuccess) {
     mine.offset = static_cast<unsigned long long>(reinterpret_cast<char *>(C) - base);
     mine.bytes = bytes;
     mine.ok = (mine.offset + bytes <= size) ? 1 : 0;
@@ -284,6 +303,9 @@ int hgemm_comm_register_output(hgemm_comm_t c, hgemm_half_t *C, size_t bytes) {
   int local_ok = ok ? 1 : 0;
   c->peer_base.assign(P, nullptr);
   c->peer_C.assign(P, nullptr);
+  c->peer_flags_base.assign(P, nullptr);
+  c->peer_flags.assign(P, nullptr);
+  c->peer_flags[me] = c->flags;
   for (int r = 0; r < P && local_ok; ++r) {
     if (!all[r].ok || all[r].bytes != bytes) local_ok = 0;
     if (r == me || !local_ok) continue;
@@ -295,6 +317,15 @@ int hgemm_comm_register_output(hgemm_comm_t c, hgemm_half_t *C, size_t bytes) {
     }
     c->peer_base[r] = pb;
     c->peer_C[r] = reinterpret_cast<hgemm_half_t *>(static_cast<char *>(pb) + all[r].offset);
+    void *fb = nullptr;
+    if (cudaIpcOpenMemHandle(&fb, all[r].flags_handle, cudaIpcMemLazyEnablePeerAccess) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      local_ok = 0;
+      break;
+    }
+    c->peer_flags_base[r] = fb;
+    c->peer_flags[r] = static_cast<unsigned long long *>(fb);
   }
   if (!C) local_ok = 0;
   int agreed = 0;
@@ -311,6 +342,13 @@ int hgemm_comm_register_output(hgemm_comm_t c, hgemm_half_t *C, size_t bytes) {
   }
   c->out_C = C;
   c->out_bytes = bytes;
+  return HGEMM_OK;
+}
+
+int hgemm_comm_output_ptr(hgemm_comm_t c, int r, hgemm_half_t **out) {
+  if (!c || !out || r < 0 || r >= c->nranks) return HGEMM_ERR_INVALID_ARG;
+  if (!c->out_C) return HGEMM_ERR_INVALID_ARG;
+  *out = (r == c->rank) ? c->out_C : c->peer_C[r];
   return HGEMM_OK;
 }
 
@@ -363,10 +401,11 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
             st = HGEMM_ERR_CUDA;
       }
     }
-    if (a.AllReduce(c->barrier_word, c->barrier_word, 1, ncclInt32, ncclMax, c->comm, s) !=
-        ncclSuccess)
-      return HGEMM_ERR_NCCL;
-    return st;
+    // Barrier: every rank announces the step in every peer's flag array and waits for
+    // theirs (a 1-warp kernel with bounded waits; its failures land in the device status
+    // word). Posted whatever happened locally, so that no peer waits in vain.
+    const int bst = hgemm_internal_peer_barrier(c->peer_flags.data(), me, P, ++c->epoch, stream);
+    return st != HGEMM_OK ? st : bst;
   }
 
   if (M % P == 0 && chunks == 1) {

@@ -75,6 +75,7 @@ enum WaitSite : unsigned {
   kSiteSchedEmpty = 7,
   kSiteSchedFull = 8,
   kSiteClc = 9,
+  kSitePeerBarrier = 10,
 };
 __device__ unsigned int g_dev_status = 0;
 
@@ -113,6 +114,7 @@ struct KParams {
   __half *C;
   unsigned long long timeout_ns;
   int sched_static;  // 1: cluster c takes tiles c, c + clusters, ...; 0: cluster launch control
+  int c_evict_first;  // 1: C stores (local and peer) are marked evict-first in L2
 };
 
 // Other destinations of every C tile (e.g. the C buffers of peer GPUs mapped into this
@@ -120,9 +122,20 @@ struct KParams {
 // delivers its rows to every rank while it computes them.
 constexpr int kMaxPeers = 7;
 struct PeerMaps {
-  CUtensorMap m[kMaxPeers];
+  CUtensorMap m[kMaxPeers];  // TMA stores (lsu == 0)
+  __half *ptr[kMaxPeers];    // same M x N row-major buffers for 16-byte stores (lsu == 1)
   int n;
+  int lsu;  // 1: the epilogue warps copy each staged chunk to the peers with 16-byte stores,
+            // so the SM's TMA unit only carries the local C and the operand loads
 };
+#ifndef HGEMM_PEER_PUSH_LSU
+#define HGEMM_PEER_PUSH_LSU 1
+#endif
+// C stores carry an L2 evict-first policy from this K on: with long main loops the A and B
+// tiles are re-read from L2 many times and the streamed C should not displace them
+// (8192^3: +1.4%); with short K the whole C fits in L2 and is written back after the
+// kernel, which evict-first would pull into the kernel (4096x8192x128: -3%).
+constexpr int kCEvictFirstMinK = 4096;
 
 // ============================================================================ device helpers
 struct WaitCtx {
@@ -658,6 +671,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int sslot = 0;
     uint32_t sph = 0;
     int c_prefetched = -1;
+    // C tiles are written once and never re-read by the GEMM (see kCEvictFirstMinK).
+    const uint64_t c_policy = ptx::l2_policy_evict_first();
+    auto store_c = [&](const CUtensorMap *m, uint32_t src, int x, int y) {
+      if (p.c_evict_first)
+        ptx::tma_store_2d_hint(m, src, x, y, c_policy);
+      else
+        ptx::tma_store_2d(m, src, x, y);
+    };
+    // Peer copies of one staged 32 x 64 chunk (rows prow0.., columns pcol..) with 16-byte
+    // stores: lane l moves row 4i + l/8, 16-byte group l%8, so every warp store writes four
+    // whole 128-byte row segments.
+    auto push_peers = [&](const uint8_t *stgp, int prow0, int pcol) {
+      const int jj = lane & 7;
+      const int gc = pcol + 8 * jj;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = 4 * i + (lane >> 3);
+        const int gr = prow0 + rr;
+        const uint4 v = *reinterpret_cast<const uint4 *>(stgp + sw128_off(rr, jj));
+        if (gr < p.M && gc < p.N) {
+          const size_t off = static_cast<size_t>(gr) * p.N + gc;
+          for (int d = 0; d < peers.n; ++d) {
+            if (p.c_evict_first)
+              ptx::st_global_v4_hint(peers.ptr[d] + off, v, c_policy);
+            else
+              *reinterpret_cast<uint4 *>(peers.ptr[d] + off) = v;
+          }
+        }
+      }
+    };
     // L2 prefetch of the C_in rows this warp will read for `tile` (TMA, no smem).
     auto prefetch_c_rows = [&](int tile_idx) {
       int ptm, ptn;
@@ -780,15 +823,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                   P[32 * ch + 4 * j + 2], P[32 * ch + 4 * j + 3]);
               ptx::fence_proxy_async_smem();
               __syncwarp();
+              const int ccol = col0 + h * (BN / 2) + ch * EPI_COLS;
               if (lane == 0) {
-                const int ccol = col0 + h * (BN / 2) + ch * EPI_COLS;
                 if (row0 < p.M && ccol < p.N) {
-                  ptx::tma_store_2d(&tmC, ptx::smem_u32(stg0) + buf, ccol, row0);
-                  for (int d = 0; d < peers.n; ++d)
-                    ptx::tma_store_2d(&peers.m[d], ptx::smem_u32(stg0) + buf, ccol, row0);
+                  store_c(&tmC, ptx::smem_u32(stg0) + buf, ccol, row0);
+                  if (!peers.lsu)
+                    for (int d = 0; d < peers.n; ++d)
+                      store_c(&peers.m[d], ptx::smem_u32(stg0) + buf, ccol, row0);
                 }
                 ptx::bulk_commit_group();
               }
+              if (peers.n > 0 && peers.lsu) push_peers(stg0 + buf, row0, ccol);
             }
           }
           if (aborted) break;
@@ -901,12 +946,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           __syncwarp();
           if (lane == 0) {
             if (row0 < p.M && ccol < p.N) {
-              ptx::tma_store_2d(&tmC, ptx::smem_u32(stg), ccol, row0);
-              for (int d = 0; d < peers.n; ++d)
-                ptx::tma_store_2d(&peers.m[d], ptx::smem_u32(stg), ccol, row0);
+              store_c(&tmC, ptx::smem_u32(stg), ccol, row0);
+              if (!peers.lsu)
+                for (int d = 0; d < peers.n; ++d)
+                  store_c(&peers.m[d], ptx::smem_u32(stg), ccol, row0);
             }
             ptx::bulk_commit_group();  // one group per chunk, empty when nothing was stored
           }
+          if (peers.n > 0 && peers.lsu) push_peers(stg, row0, ccol);
         } else {
           // C's rows are not 16-byte aligned: stage through smem, then coalesced 2-byte
           // accesses (lanes along a row), predicated on the M/N edges.
@@ -965,11 +1012,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (aborted_chunks) break;
       ++it;
     }
-    if (TMA_EPI && lane == 0) {
-      ptx::bulk_wait_group<0>();
-      // Stores into peers' memory: complete and ordered system-wide before the CTA exits.
-      if (peers.n > 0) __threadfence_system();
-    }
+    if (TMA_EPI && lane == 0) ptx::bulk_wait_group<0>();
+    // Stores into peers' memory: complete and ordered system-wide before the CTA exits.
+    if (peers.n > 0) __threadfence_system();
     __syncwarp();
   }
 
@@ -1073,6 +1118,38 @@ __global__ void wait_selftest_kernel(unsigned long long timeout_ns, int *out) {
     w.timeout_ns = timeout_ns;
     const bool ok = wait_bar<false>(ptx::smem_u32(&bar), 0u, w, kSiteSelftest);
     *out = ok ? HGEMM_OK : HGEMM_ERR_DEVICE_TIMEOUT;
+  }
+}
+
+// Cross-GPU barrier of a row-sharded step. Every rank owns an array of kMaxRanksBarrier
+// 64-bit epochs; flags[r] in rank q's array is the last step that rank r has finished (its
+// GEMM kernel, whose peer stores were completed and fenced system-wide, precedes this
+// kernel in the stream). Lane i announces the step to rank i (release store, system
+// scope, through the CUDA IPC mapping of rank i's array), then waits until rank i has
+// announced it here (acquire load), at most timeout_ns; a wait that runs out records
+// kSitePeerBarrier in the device status word and returns.
+constexpr int kMaxRanksBarrier = 8;
+struct BarrierArgs {
+  unsigned long long *flags[kMaxRanksBarrier];  // rank i's flag array as mapped here
+  int rank, nranks;
+};
+__global__ void peer_barrier_kernel(const BarrierArgs a, unsigned long long epoch,
+                                    unsigned long long timeout_ns) {
+  const int i = threadIdx.x;
+  if (i >= a.nranks || i == a.rank) return;
+  unsigned long long *remote = a.flags[i] + a.rank;
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(remote), "l"(epoch) : "memory");
+  const unsigned long long *mine = a.flags[a.rank] + i;
+  const unsigned long long t0 = ptx::globaltimer();
+  for (unsigned it = 0;; ++it) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
+    if (v >= epoch) return;
+    if ((it & 15u) == 15u && ptx::globaltimer() - t0 > timeout_ns) {
+      atomicCAS(&g_dev_status, 0u, kDevTimeout | kSitePeerBarrier);
+      return;
+    }
+    ptx::nanosleep_ns(64);
   }
 }
 
@@ -1388,8 +1465,10 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
         return HGEMM_ERR_NOT_FUSABLE;
       if (!encode_2d(&peers.m[i], peer_C[i], M, N, N, EPI_ROWS, EPI_COLS))
         return HGEMM_ERR_TENSOR_MAP;
+      peers.ptr[i] = peer_C[i];
     }
     peers.n = npeers;
+    peers.lsu = HGEMM_PEER_PUSH_LSU;
   }
   KernelFn k = kernel_for(tile, tma_epi);
   if (!d.attr_done[tile][tma_epi]) {
@@ -1414,6 +1493,8 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   kp.C = C;
   kp.timeout_ns = g_timeout_ns.load();
   kp.sched_static = pl.sched_static;
+  // Peer copies are never read on the receiving GPU during the step either.
+  kp.c_evict_first = (K >= kCEvictFirstMinK || npeers > 0) ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid_ctas, 1, 1);
@@ -1513,6 +1594,22 @@ int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *
   return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
                                 reinterpret_cast<cudaStream_t>(stream), force_bm, force_bn,
                                 group_m));
+}
+
+// Used by the multi-GPU layer only (not part of the public header).
+__attribute__((visibility("hidden"))) int hgemm_internal_peer_barrier(
+    unsigned long long *const *flags, int rank, int nranks, unsigned long long epoch,
+    hgemm_stream_t stream) {
+  if (!flags || nranks < 1 || nranks > kMaxRanksBarrier || rank < 0 || rank >= nranks)
+    return HGEMM_ERR_INVALID_ARG;
+  BarrierArgs a;
+  std::memset(&a, 0, sizeof(a));
+  for (int r = 0; r < nranks; ++r) a.flags[r] = flags[r];
+  a.rank = rank;
+  a.nranks = nranks;
+  peer_barrier_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      a, epoch, g_timeout_ns.load());
+  return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
 }
 
 int hgemm_launch_peers(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
@@ -1665,6 +1762,41 @@ int hgemm_selftest_wait_timeout(unsigned long long timeout_ns) {
   if (st != HGEMM_OK) return set_status(st);
   set_status(HGEMM_OK);
   return h;
+}
+
+int hgemm_selftest_peer_barrier(unsigned long long timeout_ns) {
+  // Rank 0 of a two-rank barrier whose partner never announces: the bounded wait must run
+  // out, record kSitePeerBarrier and return. Both flag arrays are local memory.
+  unsigned long long *d = nullptr;
+  if (cudaMalloc(&d, 2 * kMaxRanksBarrier * sizeof(unsigned long long)) != cudaSuccess)
+    return set_status(HGEMM_ERR_CUDA);
+  int st = cudaMemset(d, 0, 2 * kMaxRanksBarrier * sizeof(unsigned long long)) == cudaSuccess
+               ? HGEMM_OK
+               : HGEMM_ERR_CUDA;
+  if (st == HGEMM_OK) {
+    BarrierArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.flags[0] = d;
+    a.flags[1] = d + kMaxRanksBarrier;
+    a.rank = 0;
+    a.nranks = 2;
+    peer_barrier_kernel<<<1, 32>>>(a, 1ull, timeout_ns);
+    st = cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
+    unsigned long long announced = 0;
+    if (st == HGEMM_OK &&
+        cudaMemcpy(&announced, d + kMaxRanksBarrier, sizeof(announced),
+                   cudaMemcpyDeviceToHost) != cudaSuccess)
+      st = HGEMM_ERR_CUDA;
+    if (st == HGEMM_OK && announced != 1ull) st = HGEMM_ERR_CUDA;  // lane 1 must have announced
+  }
+  cudaFree(d);
+  int where = 0;
+  const int dev = hgemm_device_status(1, &where);  // read and clear what the test recorded
+  if (st != HGEMM_OK) return set_status(st);
+  set_status(HGEMM_OK);
+  return (dev == HGEMM_ERR_DEVICE_TIMEOUT && where == static_cast<int>(kSitePeerBarrier))
+             ? HGEMM_ERR_DEVICE_TIMEOUT
+             : HGEMM_OK;
 }
 
 void hgemm_release(void) {

@@ -190,6 +190,27 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap *m, uint32_t 
       "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1)
       : "memory");
 }
+// L2 policy that marks lines as the first to evict (streamed output that no CTA re-reads).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap *m, uint32_t src, int32_t c0,
+                                                  int32_t c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3}], [%1], %4;" ::"l"(reinterpret_cast<uint64_t>(m)),
+      "r"(src), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+// 16-byte global store with an L2 policy (and no L1 allocation).
+__device__ __forceinline__ void st_global_v4_hint(void *ptr, uint4 v, uint64_t policy) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(
+                   ptr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "l"(policy)
+               : "memory");
+}
 // Asks the TMA unit to bring a 2-D box into L2 (no shared memory, no completion signal).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *m, int32_t c0, int32_t c1) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(

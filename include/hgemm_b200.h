@@ -112,6 +112,12 @@ void hgemm_set_wait_timeout_ns(unsigned long long ns);
  * the bound works). Leaves the CUDA context usable; clears the device status word. */
 int hgemm_selftest_wait_timeout(unsigned long long timeout_ns);
 
+/* Self-test of the multi-GPU barrier's bounded wait (one GPU, local memory only): runs the
+ * barrier kernel as rank 0 of two with a partner that never announces. Returns
+ * HGEMM_ERR_DEVICE_TIMEOUT when the wait gave up after ~timeout_ns and recorded its site
+ * (the expected outcome), HGEMM_OK if it did not. Clears the device status word. */
+int hgemm_selftest_peer_barrier(unsigned long long timeout_ns);
+
 /* Frees the per-device scratch used to restride A (K % 8 != 0) or B (N % 8 != 0). */
 void hgemm_release(void);
 
@@ -179,6 +185,11 @@ int hgemm_comm_destroy(hgemm_comm_t comm);
  * only when every rank registered (the outcome is agreed on collectively). No counterpart
  * in the reference. */
 int hgemm_comm_register_output(hgemm_comm_t comm, hgemm_half_t *C, size_t bytes);
+
+/* Address, in this process, of rank r's registered output buffer (this rank's own C for
+ * r == rank; a CUDA IPC mapping opened on this rank's device otherwise), or
+ * HGEMM_ERR_INVALID_ARG when no output is registered. No counterpart in the reference. */
+int hgemm_comm_output_ptr(hgemm_comm_t comm, int r, hgemm_half_t **out);
 
 /* SMs that the chunk GEMMs of hgemm_sharded_rank (chunks > 1, nranks > 1) leave free for
  * the exchange kernels that run next to them (default 16; 0 = the GEMM takes every SM).

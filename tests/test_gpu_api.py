@@ -110,5 +110,18 @@ def test_bounded_wait_gives_up_and_context_survives(cuda, oracle):
     assert ok, worst
 
 
+def test_peer_barrier_wait_gives_up(cuda, oracle):
+    """The multi-GPU step barrier waits on a flag that only a peer GPU writes; with a partner
+    that never announces, its bounded wait must give up, record its site and leave the
+    context usable (one GPU, local memory only)."""
+    st = cuda.lib.hgemm_selftest_peer_barrier(5_000_000)  # 5 ms
+    assert st == cuda.HGEMM_ERR_DEVICE_TIMEOUT
+    assert cuda.device_status(clear=True)[0] == 0
+    A, B, _ = _inputs(oracle, 128, 64, 64, seed=10)
+    out = host(cuda.gemm(dev(A), dev(B)))
+    ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B), 64)
+    assert ok, worst
+
+
 def test_device_status_clean(cuda):
     assert cuda.device_status(clear=False)[0] == 0
