@@ -29,7 +29,7 @@ class HgemmPlan(ctypes.Structure):
                 ("tiles_m", ctypes.c_int), ("tiles_n", ctypes.c_int),
                 ("grid_ctas", ctypes.c_int), ("pad_a", ctypes.c_int), ("pad_b", ctypes.c_int),
                 ("lda", ctypes.c_int), ("ldb", ctypes.c_int), ("tma_store", ctypes.c_int),
-                ("scratch_bytes", ctypes.c_size_t), ("sched_static", ctypes.c_int)]
+                ("scratch_bytes", ctypes.c_size_t), ("sched_static", ctypes.c_int), ("ksplit", ctypes.c_int)]
 
     def as_dict(self):
         return {name: getattr(self, name) for name, _ in self._fields_}
@@ -47,6 +47,7 @@ SIGNATURES = {
     "hgemm_launch_ex": (_i, _GEMM + [_vp, _i, _i, _i]),
     "hgemm_launch_tuned": (_i, _GEMM + [_vp]),
     "hgemm_launch_sm_limit": (_i, _GEMM + [_vp, _i]),
+    "hgemm_launch_splitk": (_i, _GEMM + [_vp, _i, _i]),
     "hgemm_launch_peers": (_i, _GEMM + [_vp, _vp, _i, _i]),
     "hgemm_launch_noalloc": (_i, _GEMM + [_vp]),
     "hgemm_noalloc_scratch_bytes": (ctypes.c_size_t, []),

@@ -60,6 +60,8 @@ constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in dynamic shared memory per b
 constexpr int BAR_BYTES = 512;
 // Peer-store launches keep the 256x512 tile only from this K on (longer main loop per tile).
 constexpr int kPeerWideTileMinK = 12288;
+// Largest split-K cluster (portable cluster size).
+constexpr int kMaxSplit = 8;
 // Tiles whose main loop is estimated shorter than this (cycles) use the static schedule.
 constexpr double kStaticTileCycles = 8192.0;
 
@@ -76,6 +78,7 @@ enum WaitSite : unsigned {
   kSiteSchedFull = 8,
   kSiteClc = 9,
   kSitePeerBarrier = 10,
+  kSiteSplitReduce = 11,
 };
 __device__ unsigned int g_dev_status = 0;
 
@@ -115,6 +118,8 @@ struct KParams {
   unsigned long long timeout_ns;
   int sched_static;  // 1: cluster c takes tiles c, c + clusters, ...; 0: cluster launch control
   int c_evict_first;  // 1: C stores (local and peer) are marked evict-first in L2
+  int ksplit;         // > 1 (one-CTA tiles only): a cluster of ksplit CTAs shares each tile's
+                      // k-blocks and reduces the partial sums over distributed shared memory
 };
 
 // Other destinations of every C tile (e.g. the C buffers of peer GPUs mapped into this
@@ -244,8 +249,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t *sched_full = bars + 2 * S + 5;  // [NSL] tile index written
   uint64_t *sched_empty = bars + 2 * S + 5 + NSL;  // [NSL] every reader took it (leader's copy)
   uint64_t *clc_bar = bars + 2 * S + 5 + 2 * NSL;  // [1]  launch-control response landed
+  uint64_t *red_ready = bars + 2 * S + 6 + 2 * NSL;  // [1] split-K: every partial is in smem
+  uint64_t *red_done = bars + 2 * S + 7 + 2 * NSL;   // [1] split-K: nobody reads ours any more
   uint8_t *misc = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(bars + 2 * S + 6 + 2 * NSL) + 15) & ~uintptr_t(15));
+      (reinterpret_cast<uintptr_t>(bars + 2 * S + 8 + 2 * NSL) + 15) & ~uintptr_t(15));
   uint8_t *clc_resp = misc;                                      // 16 bytes
   volatile int *sched_val = reinterpret_cast<volatile int *>(misc + 16);  // [NSL]
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(misc + 16 + 4 * NSL);
@@ -254,7 +261,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = (PAIR == 2) ? ptx::cluster_ctarank() : 0u;
-  const int first_tile = (PAIR == 2) ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
+  // Split-K (one-CTA tiles): the cluster's CTAs share one tile, CTA `split` taking k-blocks
+  // [kb_begin, kb_end).
+  const int ksplit = (PAIR == 1 && p.ksplit > 1) ? p.ksplit : 1;
+  const int split = ksplit > 1 ? static_cast<int>(ptx::cluster_ctarank()) : 0;
+  const int kb_begin = static_cast<int>(static_cast<long long>(p.num_kb) * split / ksplit);
+  const int kb_end = static_cast<int>(static_cast<long long>(p.num_kb) * (split + 1) / ksplit);
+  const bool clustered = PAIR == 2 || ksplit > 1;
+  const int first_tile =
+      clustered ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -273,6 +288,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ptx::mbar_init(ptx::smem_u32(&sched_empty[i]), PAIR == 2 ? 10 : 5);
     }
     ptx::mbar_init(ptx::smem_u32(clc_bar), 1);
+    // Split-K: each of the cluster's 4 * ksplit epilogue warps arrives once on every CTA.
+    ptx::mbar_init(ptx::smem_u32(red_ready), 4 * ksplit);
+    ptx::mbar_init(ptx::smem_u32(red_done), 4 * ksplit);
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
   }
@@ -290,7 +308,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (PAIR == 2) ptx::cluster_sync();
+  if (clustered) ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_holder);
 
@@ -347,7 +365,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         decode_tile(tile, p, tm, tn);
         const int arow = tm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M;
         const int bcol = tn * BN + static_cast<int>(rank) * Cfg::SUB_COLS;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!wait_bar<false>(ptx::smem_u32(&empty[s]), ph ^ 1u, wctx, kSiteProducerEmpty))
             return false;
           const uint32_t fbar = full_leader0 + static_cast<uint32_t>(s) * 8u;
@@ -400,7 +418,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           return true;
         };
         bool clc_live = p.sched_static == 0, clc_pending = false;
-        const int stride = (PAIR == 2) ? static_cast<int>(ptx::nclusters_x()) : static_cast<int>(gridDim.x);
+        const int stride =
+            clustered ? static_cast<int>(ptx::nclusters_x()) : static_cast<int>(gridDim.x);
         uint32_t clc_ph = 0;
         int tile = first_tile;
         ok = publish(tile);
@@ -493,7 +512,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ptx::umma_f16<PAIR>(dtm + static_cast<uint32_t>(j * Cfg::UMMA_N),
                               adesc + static_cast<uint64_t>(2 * k),
                               bdesc + static_cast<uint64_t>(128 * k + j * Cfg::SUB_BOXES * (BK * 128 / 16)),
-                              idesc, (kb | k) != 0 ? 1u : 0u);
+                              idesc, ((kb - kb_begin) | k) != 0 ? 1u : 0u);
         issued_any = true;
       };
       auto release_stage = [&](int stage) {
@@ -512,7 +531,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int next = -1;
         bool have_next = false;
         auto poll_next = [&](int kb) {
-          if (!have_next && kb >= p.num_kb - S && sched_try_read(sslot, sph, next)) have_next = true;
+          if (!have_next && kb >= kb_end - S && sched_try_read(sslot, sph, next)) have_next = true;
         };
         const int acc = it % ACC_BUFS;
         const uint32_t aph = static_cast<uint32_t>(it / ACC_BUFS) & 1u;
@@ -526,7 +545,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // One issuing thread has only ~4 UMMAs' time (BN=256) per k-block, so the hot loop
           // carries nothing but the wait, the UMMAs and the stage release; the look-ahead on
           // the tile ring happens in a separate tail loop over the last S k-blocks.
-          const int main_kb = p.num_kb > S ? p.num_kb - S : 0;
+          const int main_kb = kb_end - S > kb_begin ? kb_end - S : kb_begin;
           auto kblock = [&](int kb) -> bool {
             if (!wait_bar<false>(ptx::smem_u32(&full[s]), ph, wctx, kSiteMmaFull)) return false;
             ptx::tc_fence_after();
@@ -539,8 +558,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             return true;
           };
-          for (int kb = 0; kb < main_kb && ok; ++kb) ok = kblock(kb);
-          for (int kb = main_kb; kb < p.num_kb && ok; ++kb) {
+          for (int kb = kb_begin; kb < main_kb && ok; ++kb) ok = kblock(kb);
+          for (int kb = main_kb; kb < kb_end && ok; ++kb) {
             ok = kblock(kb);
             poll_next(kb);
           }
@@ -756,6 +775,127 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (okk) ptx::tc_fence_after();
         return okk != 0;
       };
+      if (PAIR == 1 && TMA_EPI && ksplit > 1) {
+        // ---- split-K: one tile per cluster, CTA `split` holds the sums of its k-blocks.
+        // (1) partial sums -> this CTA's shared memory, fp32 (the pipeline stages are free:
+        //     every UMMA of the cluster's only tile has retired). Row r (tile-local) starts
+        //     at r * BN * 4 bytes; its 16-byte group g is stored at g ^ (r & 7).
+        const uint32_t part = sA0;
+        const int r_loc = EPI_ROWS * q + lane;
+        const uint32_t prow = part + static_cast<uint32_t>(r_loc) * (BN * 4);
+        const uint32_t rsw = static_cast<uint32_t>(r_loc & 7);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c += 2) {
+          uint32_t v[64];
+          ptx::tmem_ld_32x32b_x32(tbase + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+          ptx::tmem_ld_32x32b_x32(tbase + 32 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t g = static_cast<uint32_t>(8 * c + j);
+            ptx::st_shared_v4(prow + ((g ^ rsw) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                              v[4 * j + 3]);
+          }
+        }
+        // (2) announce this warp's rows to every CTA of the cluster, then wait for all of
+        //     theirs (bounded).
+        ptx::tc_fence_before();
+        ptx::fence_acq_rel_cluster();
+        __syncwarp();
+        if (lane == 0)
+          for (int t = 0; t < ksplit; ++t)
+            ptx::mbar_arrive_cluster(ptx::mapa(ptx::smem_u32(red_ready), static_cast<uint32_t>(t)));
+        int okr = 1;
+        if (lane == 0)
+          okr = wait_bar<true>(ptx::smem_u32(red_ready), 0u, wctx, kSiteSplitReduce) ? 1 : 0;
+        okr = __shfl_sync(0xffffffffu, okr, 0);
+        ptx::fence_acq_rel_cluster();
+        // (3) reduce-scatter: the tile's (128/32) x (BN/64) chunks of 32 x 64 go round robin
+        //     to the cluster's 4 * ksplit epilogue warps; each sums the ksplit partials of its
+        //     chunk in split order (fixed, so results are bit-stable), applies alpha / beta,
+        //     rounds once to half and TMA-stores the chunk. Reads are coalesced: lanes
+        //     16h..16h+15 take one row's 64 columns (256 contiguous bytes), so a warp load
+        //     covers two rows; lane l holds rows 2i + l/16 (i < 16), columns 4(l%16)..+3.
+        const int workers = 4 * ksplit;
+        const int lhalf = lane >> 4, lg = lane & 15;
+#pragma unroll 1
+        for (int ci = 4 * split + q; okr && ci < 4 * (BN / 64); ci += workers) {
+          const int rb = ci & 3, cb = ci >> 2;
+          float f[64];
+#pragma unroll 1
+          for (int t = 0; t < ksplit; ++t) {
+            const uint32_t tb = (t == split) ? part : ptx::mapa(part, static_cast<uint32_t>(t));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int rr = 32 * rb + 2 * i + lhalf;
+              const uint32_t g = static_cast<uint32_t>(16 * cb + lg);
+              const uint32_t a = tb + static_cast<uint32_t>(rr) * (BN * 4) +
+                                 ((g ^ static_cast<uint32_t>(rr & 7)) << 4);
+              const float4 x = (t == split) ? ptx::ld_shared_v4f(a) : ptx::ld_shared_cluster_v4f(a);
+              if (t == 0) {
+                f[4 * i] = x.x; f[4 * i + 1] = x.y; f[4 * i + 2] = x.z; f[4 * i + 3] = x.w;
+              } else {
+                f[4 * i] += x.x; f[4 * i + 1] += x.y; f[4 * i + 2] += x.z; f[4 * i + 3] += x.w;
+              }
+            }
+          }
+          const int gcol = col0 + 64 * cb + 4 * lg;  // this lane's first column
+#pragma unroll
+          for (int e = 0; e < 64; ++e) f[e] *= alpha;
+          if (beta != 0.0f) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int grow = tm * CTA_M + 32 * rb + 2 * i + lhalf;
+              if (grow < p.M && gcol < p.N) {  // N % 8 == 0: 4 halves wholly inside or outside
+                const uint2 u = __ldg(reinterpret_cast<const uint2 *>(
+                    p.C + static_cast<long long>(grow) * p.N + gcol));
+                const float2 c0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+                const float2 c1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+                f[4 * i] = fmaf(beta, c0.x, f[4 * i]);
+                f[4 * i + 1] = fmaf(beta, c0.y, f[4 * i + 1]);
+                f[4 * i + 2] = fmaf(beta, c1.x, f[4 * i + 2]);
+                f[4 * i + 3] = fmaf(beta, c1.y, f[4 * i + 3]);
+              }
+            }
+          }
+          uint8_t *stg = stg0 + (chunk_ctr & 1) * (EPI_ROWS * 128);
+          ++chunk_ctr;
+          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          __syncwarp();
+          // staging layout of the TMA store: row r's 16-byte group j at r*128 + (j ^ (r&7))*16;
+          // this lane's 4 halves are the (lg&1) half of group lg/2.
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int r = 2 * i + lhalf;
+            uint2 w;
+            w.x = pack_half2(f[4 * i], f[4 * i + 1]);
+            w.y = pack_half2(f[4 * i + 2], f[4 * i + 3]);
+            *reinterpret_cast<uint2 *>(stg + sw128_off(r, lg >> 1) + 8 * (lg & 1)) = w;
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int srow = tm * CTA_M + 32 * rb;
+            const int scol = col0 + 64 * cb;
+            if (srow < p.M && scol < p.N) store_c(&tmC, ptx::smem_u32(stg), scol, srow);
+            ptx::bulk_commit_group();
+          }
+        }
+        // (4) this warp no longer reads any CTA's partials: tell every CTA, and do not let
+        //     this CTA exit (freeing its shared memory) before the whole cluster is done.
+        ptx::fence_acq_rel_cluster();
+        __syncwarp();
+        if (lane == 0)
+          for (int t = 0; t < ksplit; ++t)
+            ptx::mbar_arrive_cluster(ptx::mapa(ptx::smem_u32(red_done), static_cast<uint32_t>(t)));
+        int okd = 1;
+        if (lane == 0)
+          okd = wait_bar<true>(ptx::smem_u32(red_done), 0u, wctx, kSiteSplitReduce) ? 1 : 0;
+        okd = __shfl_sync(0xffffffffu, okd, 0);
+        if (!okr || !okd) break;
+        ++it;
+        continue;
+      }
       if constexpr (ACC_BUFS == 1 && TMA_EPI) {
         if (beta == 0.0f) {
           // Single accumulator: drain each N half into registers as packed halves, give that
@@ -1022,7 +1162,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (*abort_flag) ptx::nanosleep_ns(20000);  // unwinding: let stray copies land
   ptx::tc_fence_before();
   __syncthreads();
-  if (PAIR == 2) ptx::cluster_sync();
+  if (clustered) ptx::cluster_sync();
   if (warp == 1) {
     __syncwarp();
     ptx::tc_fence_after();
@@ -1305,10 +1445,13 @@ int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b
 // enough to stay in the 126 MB L2.
 int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int force_bn,
               int group_m, int sm_count, int pair_slots, hgemm_plan_t *pl,
-              bool persistent_only = false) {
+              bool persistent_only = false, int ksplit_req = 0) {
   std::memset(pl, 0, sizeof(*pl));
   if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
   if ((force_bm != 0 || force_bn != 0) && tile_from_force(force_bm, force_bn) < 0)
+    return HGEMM_ERR_INVALID_ARG;
+  if (ksplit_req < 0 || ksplit_req > kMaxSplit ||
+      (ksplit_req > 1 && (force_bm != CTA_M || force_bn == 0)))
     return HGEMM_ERR_INVALID_ARG;
   if (sm_count <= 0) sm_count = 148;
   if (pair_slots <= 0) pair_slots = sm_count / 2;
@@ -1397,6 +1540,49 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   pl->sched_static =
       (persistent_only || total <= slots || tile_cycles < kStaticTileCycles) ? 1 : 0;
   pl->grid_ctas = static_cast<int>((pl->sched_static ? units : total) * ti.pair);
+  pl->ksplit = 1;
+
+  // Split-K. When the tiles occupy only a few SMs, each CTA walks all of K with only its
+  // stages in flight (TMA-latency bound); a cluster of ksplit one-CTA tiles then shares each
+  // tile's k-blocks and reduces over distributed shared memory. The reduction and its two
+  // cluster-wide waits cost ~9 K cycles (B200, 1024^3 split 2: 19.8 us against 17.5 us
+  // unsplit), so it is chosen only for grids that fill at most a quarter of the SMs. Needs the
+  // TMA-store epilogue; at least 4 k-blocks per split.
+  const int kbn = ceil_div(K, BK);
+  int ks = 1, ks_tile = -1;
+  if (ksplit_req > 1) {
+    ks = std::min(ksplit_req, kbn);
+    ks_tile = tile;
+  } else if (ksplit_req == 0 && force_bm == 0 && !persistent_only && pl->tma_store) {
+    const long long ctas_used = static_cast<long long>(units) * ti.pair;
+    if (ctas_used * 4 <= static_cast<long long>(sm_count)) {
+      long long best_ctas = ctas_used;
+      for (int t : {kT128x256, kT128x128, kT128x64}) {
+        const long long tt = static_cast<long long>(ceil_div(M, CTA_M)) * ceil_div(N, kTiles[t].bn);
+        const int k = static_cast<int>(std::min<long long>(
+            {static_cast<long long>(kMaxSplit), sm_count / std::max(tt, 1LL), kbn / 4}));
+        if (k >= 2 && tt * k > best_ctas) {
+          best_ctas = tt * k;
+          ks = k;
+          ks_tile = t;
+        }
+      }
+    }
+  }
+  if (ks > 1 && pl->tma_store) {
+    const TileInfo &st = kTiles[ks_tile];
+    pl->pair = 1;
+    pl->tile_m = CTA_M;
+    pl->tile_n = st.bn;
+    pl->stages = st.stages;
+    pl->tiles_m = ceil_div(M, CTA_M);
+    pl->tiles_n = ceil_div(N, st.bn);
+    pl->ksplit = ks;
+    pl->sched_static = 1;
+    pl->grid_ctas = pl->tiles_m * pl->tiles_n * ks;
+    pl->group_m = 1;
+    return HGEMM_OK;
+  }
   if (group_m == 0) {
     // Working set of one wave ~ g tile-rows of A plus (units/g) tile-columns of B; choose g
     // near sqrt(units * tile_n / tile_m) (equal A and B footprints), at least 1.
@@ -1493,6 +1679,7 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   kp.C = C;
   kp.timeout_ns = g_timeout_ns.load();
   kp.sched_static = pl.sched_static;
+  kp.ksplit = pl.ksplit > 1 ? pl.ksplit : 1;
   // Peer copies are never read on the receiving GPU during the step either.
   kp.c_evict_first = (K >= kCEvictFirstMinK || npeers > 0) ? 1 : 0;
 
@@ -1503,11 +1690,11 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = ti.pair;
+  attr[0].val.clusterDim.x = ti.pair == 2 ? 2 : kp.ksplit;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = ti.pair == 2 ? 1 : 0;
+  cfg.numAttrs = (ti.pair == 2 || kp.ksplit > 1) ? 1 : 0;
   if (cudaLaunchKernelEx(&cfg, k, ta, tb, tc, kp, peers) != cudaSuccess) {
     cudaGetLastError();
     return HGEMM_ERR_LAUNCH;
@@ -1517,7 +1704,8 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
 
 int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K, float alpha,
                 float beta, cudaStream_t stream, int force_bm, int force_bn, int group_m,
-                int sm_limit = 0, __half *const *peer_C = nullptr, int npeers = 0) {
+                int sm_limit = 0, __half *const *peer_C = nullptr, int npeers = 0,
+                int ksplit_req = 0) {
   if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return HGEMM_OK;
   if (!A || !B || !C) return HGEMM_ERR_INVALID_ARG;
@@ -1536,8 +1724,9 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
     pslots = std::max(1, std::min(pslots, sm_limit / 2));
   }
   hgemm_plan_t pl;
+  // Peer stores are issued by the tile's own epilogue, which split-K replaces.
   st = make_plan(M, N, K, beta, aligned16, force_bm, force_bn, group_m, sms, pslots, &pl,
-                 sm_limit > 0);
+                 sm_limit > 0, npeers > 0 ? 1 : ksplit_req);
   if (st != HGEMM_OK) return st;
   if (pl.path == 0) return HGEMM_OK;
   if (npeers > 0 && (pl.path != 1 || !pl.tma_store)) return HGEMM_ERR_NOT_FUSABLE;
@@ -1546,7 +1735,8 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
     // accumulator that longer epilogue sits between tiles; the double-buffered 256x256 tile
     // hides it behind the next tile's main loop (measured on 2 B200s: faster at K = 8192,
     // slower at K = 16384).
-    st = make_plan(M, N, K, beta, aligned16, 256, 256, group_m, sms, pslots, &pl, sm_limit > 0);
+    st = make_plan(M, N, K, beta, aligned16, 256, 256, group_m, sms, pslots, &pl, sm_limit > 0,
+                   1);
     if (st != HGEMM_OK) return st;
   }
   if (pl.path == 2) return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
@@ -1620,6 +1810,16 @@ int hgemm_launch_peers(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_
   return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
                                 reinterpret_cast<cudaStream_t>(stream), 0, 0, 0,
                                 sm_limit > 0 ? sm_limit : 0, peer_C, npeers));
+}
+
+int hgemm_launch_splitk(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                        int N, int K, float alpha, float beta, hgemm_stream_t stream, int bn,
+                        int ksplit) {
+  if (ksplit < 1 || ksplit > kMaxSplit || (bn != 64 && bn != 128 && bn != 256))
+    return set_status(HGEMM_ERR_INVALID_ARG);
+  return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
+                                reinterpret_cast<cudaStream_t>(stream), CTA_M, bn, 0, 0, nullptr,
+                                0, ksplit));
 }
 
 int hgemm_launch_sm_limit(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,

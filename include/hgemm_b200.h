@@ -139,6 +139,16 @@ int hgemm_launch_peers(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_
                        int N, int K, float alpha, float beta, hgemm_stream_t stream,
                        hgemm_half_t *const *peer_C, int npeers, int sm_limit);
 
+/* Forces the one-CTA 128 x bn tile (bn = 64, 128 or 256) split over `ksplit` (1..8) CTAs
+ * along K: each cluster of ksplit CTAs computes one tile, every CTA summing a contiguous
+ * range of k-blocks, and the partial sums are reduced in a fixed order over distributed
+ * shared memory (bit-stable). Shapes without the TMA-store epilogue (N % 8 != 0) run
+ * unsplit. hgemm_launch picks split-K by itself for small problems. No counterpart in the
+ * reference. */
+int hgemm_launch_splitk(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
+                        int N, int K, float alpha, float beta, hgemm_stream_t stream, int bn,
+                        int ksplit);
+
 /* Host-only description of what hgemm_launch_ex would run; needs no GPU. */
 typedef struct {
   int path;       /* 0 no-op, 1 tcgen05 tiles, 2 SIMT fallback */
@@ -157,6 +167,8 @@ typedef struct {
   size_t scratch_bytes;  /* scratch needed for restrided operands */
   int sched_static;      /* 1: cluster c takes tiles c, c + clusters, ... (short tiles, or all
                             tiles co-resident); 0: cluster launch control */
+  int ksplit;            /* > 1: split-K, a cluster of ksplit one-CTA tiles shares each tile's
+                            k-blocks (grid_ctas = tiles * ksplit) */
 } hgemm_plan_t;
 
 /* `aligned16` says whether A, B and C all start on 16-byte boundaries; `sm_count` and

@@ -44,8 +44,11 @@ def test_large_square_uses_widest_pair_tile():
 
 def test_small_problem_spreads_over_sms():
     p = hg.plan(1024, 1024, 1024, **B200)
-    tiles = p["tiles_m"] * p["tiles_n"]
-    assert tiles * p["pair"] >= 64  # uses at least 64 SMs
+    assert p["grid_ctas"] >= 64  # uses at least 64 SMs
+    # a handful of tiles would leave most SMs idle: split-K clusters of one-CTA tiles
+    p = hg.plan(256, 256, 4096, **B200)
+    assert p["ksplit"] > 1 and p["pair"] == 1
+    assert p["grid_ctas"] == p["tiles_m"] * p["tiles_n"] * p["ksplit"] <= 148
 
 
 @pytest.mark.parametrize("bm,bn", [(256, 512), (256, 256), (256, 128), (128, 256), (128, 128),
@@ -67,7 +70,7 @@ def test_invalid_forced_tile_rejected():
 def test_grid_is_one_cluster_per_tile():
     for M, N, K in [(16384, 16384, 16384), (384, 2048, 2048), (1, 4096, 4096), (8192, 8, 8192)]:
         p = hg.plan(M, N, K, **B200)
-        assert p["grid_ctas"] == p["tiles_m"] * p["tiles_n"] * p["pair"]
+        assert p["grid_ctas"] == p["tiles_m"] * p["tiles_n"] * p["pair"] * p["ksplit"]
 
 
 def test_schedule_choice():
@@ -80,6 +83,21 @@ def test_schedule_choice():
     slots = B200["pair_slots"] if p["pair"] == 2 else B200["sm_count"]
     assert p["grid_ctas"] == min(p["tiles_m"] * p["tiles_n"], slots) * p["pair"]
     # every tile co-resident: static, one cluster per tile
-    p = hg.plan(1024, 1024, 1024, **B200)
-    assert p["sched_static"] == 1
+    p = hg.plan(2048, 2048, 2048, **B200)
+    assert p["sched_static"] == 1 and p["ksplit"] == 1
     assert p["grid_ctas"] == p["tiles_m"] * p["tiles_n"] * p["pair"]
+
+
+def test_split_k_choice():
+    # big enough to fill the machine: never split
+    for shape in [(8192, 8192, 8192), (4096, 8192, 128), (2048, 2048, 512), (1024, 1024, 1024),
+                  (384, 2048, 2048)]:
+        assert hg.plan(*shape, **B200)["ksplit"] == 1
+    # a handful of tiles: split, at most 8 per cluster, at least 4 k-blocks per split
+    for M, N, K in [(256, 256, 4096), (128, 128, 8192), (512, 512, 8192)]:
+        p = hg.plan(M, N, K, **B200)
+        assert 2 <= p["ksplit"] <= 8 and p["pair"] == 1
+        assert (K + 63) // 64 >= 4 * p["ksplit"]
+        assert p["grid_ctas"] <= 148
+    # ragged N has no TMA-store epilogue: no split
+    assert hg.plan(384, 2046, 2048, **B200)["ksplit"] == 1
