@@ -32,6 +32,10 @@
 
 #include "hgemm_b200.h"
 
+// GEMM that never uses split-K (hgemm_sm100.cu; internal to this library).
+extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_launch_unsplit(
+    const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
+    float alpha, float beta, hgemm_stream_t stream, int sm_limit);
 // Cross-GPU flag barrier (hgemm_sm100.cu; internal to this library).
 extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_peer_barrier(
     unsigned long long *const *flags, int rank, int nranks, unsigned long long epoch,
@@ -394,7 +398,7 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
       st = hgemm_launch_peers(A_local, B, Cl, rc, N, K, alpha, beta, stream, peers, n, 0);
       if (st == HGEMM_ERR_NOT_FUSABLE) {
         // Shapes without TMA stores: compute locally, then push the rows with copies.
-        st = hgemm_launch_ex(A_local, B, Cl, rc, N, K, alpha, beta, stream, 0, 0, 0);
+        st = hgemm_internal_launch_unsplit(A_local, B, Cl, rc, N, K, alpha, beta, stream, 0);
         for (int i = 0; i < n && st == HGEMM_OK; ++i)
           if (cudaMemcpyAsync(peers[i], Cl, static_cast<size_t>(rc) * row_elems * 2,
                               cudaMemcpyDeviceToDevice, s) != cudaSuccess)
@@ -411,8 +415,8 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
   if (M % P == 0 && chunks == 1) {
     int st = HGEMM_OK;
     if (rc > 0)
-      st = hgemm_launch_ex(A_local, B, C + static_cast<size_t>(rb) * row_elems, rc, N, K, alpha,
-                           beta, stream, 0, 0, 0);
+      st = hgemm_internal_launch_unsplit(A_local, B, C + static_cast<size_t>(rb) * row_elems, rc,
+                                         N, K, alpha, beta, stream, 0);
     if (st != HGEMM_OK) return st;
     if (P > 1 && a.AllGather(C + static_cast<size_t>(rb) * row_elems, C,
                              static_cast<size_t>(rc) * row_elems, ncclFloat16, c->comm,
@@ -433,9 +437,9 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
       const hgemm_half_t *Ac = A_local + static_cast<size_t>(cb) * K;
       hgemm_half_t *Cc = C + static_cast<size_t>(rb + cb) * row_elems;
       const int limit = c->sm_count - c->reserved_sms;
-      const int st = (P > 1 && c->reserved_sms > 0 && limit > 0)
-                         ? hgemm_launch_sm_limit(Ac, B, Cc, cn, N, K, alpha, beta, stream, limit)
-                         : hgemm_launch_ex(Ac, B, Cc, cn, N, K, alpha, beta, stream, 0, 0, 0);
+      const int st = hgemm_internal_launch_unsplit(
+          Ac, B, Cc, cn, N, K, alpha, beta, stream,
+          (P > 1 && c->reserved_sms > 0 && limit > 0) ? limit : 0);
       if (st != HGEMM_OK) return st;
     }
     if (P == 1) continue;

@@ -55,7 +55,7 @@ constexpr int CTA_M = 128;      // accumulator rows per CTA (= TMEM lanes)
 constexpr int UMMA_K = 16;      // k per tcgen05.mma.kind::f16
 constexpr int EPI_ROWS = 32;    // rows per epilogue warp (its TMEM lane quarter)
 constexpr int EPI_COLS = 64;    // columns per epilogue chunk (one 128-byte swizzle row)
-constexpr int NUM_THREADS = 192;
+
 constexpr int SMEM_LIMIT = 232448;  // sm_100 opt-in dynamic shared memory per block
 constexpr int BAR_BYTES = 512;
 // Peer-store launches keep the 256x512 tile only from this K on (longer main loop per tile).
@@ -82,6 +82,9 @@ enum WaitSite : unsigned {
 };
 __device__ unsigned int g_dev_status = 0;
 
+#ifndef HGEMM_EPI_WARPS_WIDE
+#define HGEMM_EPI_WARPS_WIDE 8
+#endif
 template <int PAIR, int BN>
 struct TileCfg {
   static constexpr int UMMA_N = BN < 256 ? BN : 256;        // N of one tcgen05.mma
@@ -94,7 +97,14 @@ struct TileCfg {
   static constexpr int B_BYTES = B_COLS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TX_BYTES = STAGE_BYTES * PAIR;        // armed on the leader's barrier
-  static constexpr int EPI_BYTES = 4 * 2 * EPI_ROWS * 128;   // 4 warps x 2 buffers x 4 KB
+  // Epilogue warps: 8 for the 128- and 256-column tiles (two per TMEM lane quarter, each
+  // taking half of the columns, so one warp's store waits overlap the other's conversions),
+  // 4 for the others. Staging: 32 KB either way (4 warps x 2 buffers or 8 x 1 of 4 KB).
+  static constexpr int EPI_WARPS = (BN == 128 || BN == 256) ? HGEMM_EPI_WARPS_WIDE : 4;
+  static constexpr int EPI_BUFS = 8 / EPI_WARPS;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int EPI_COLS_PER_WARP = BN * 4 / EPI_WARPS;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_ROWS * 128;
   static constexpr int STAGES_FIT = (SMEM_LIMIT - EPI_BYTES - 1024 - BAR_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
@@ -223,7 +233,7 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int j) {
 // publishes every tile index through a small shared-memory ring that the other roles of
 // both CTAs read; -1 ends the sequence.
 template <int PAIR, int BN, bool TMA_EPI>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
     hgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const KParams p,
                     const __grid_constant__ PeerMaps peers) {
@@ -278,19 +288,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(ptx::smem_u32(&tfull[a]), 1);
-      ptx::mbar_init(ptx::smem_u32(&tempty[a]), 4 * PAIR);
+      ptx::mbar_init(ptx::smem_u32(&tempty[a]), Cfg::EPI_WARPS * PAIR);
     }
     ptx::mbar_init(ptx::smem_u32(drain), 1);
-    // Readers of each tile index: leader MMA + 4 epilogue warps (+ the peer's producer and
-    // 4 epilogue warps for a pair).
+    // Readers of each tile index: leader MMA + the epilogue warps (+ the peer's producer and
+    // epilogue warps for a pair).
     for (int i = 0; i < NSL; ++i) {
       ptx::mbar_init(ptx::smem_u32(&sched_full[i]), 1);
-      ptx::mbar_init(ptx::smem_u32(&sched_empty[i]), PAIR == 2 ? 10 : 5);
+      ptx::mbar_init(ptx::smem_u32(&sched_empty[i]), (1 + Cfg::EPI_WARPS) * PAIR);
     }
     ptx::mbar_init(ptx::smem_u32(clc_bar), 1);
-    // Split-K: each of the cluster's 4 * ksplit epilogue warps arrives once on every CTA.
-    ptx::mbar_init(ptx::smem_u32(red_ready), 4 * ksplit);
-    ptx::mbar_init(ptx::smem_u32(red_done), 4 * ksplit);
+    // Split-K: each of the cluster's EPI_WARPS * ksplit epilogue warps arrives once on every
+    // CTA.
+    ptx::mbar_init(ptx::smem_u32(red_ready), Cfg::EPI_WARPS * ksplit);
+    ptx::mbar_init(ptx::smem_u32(red_done), Cfg::EPI_WARPS * ksplit);
     *abort_flag = 0;
     ptx::fence_mbar_init_cluster();
   }
@@ -681,7 +692,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue warps
     const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are the ones this warp may read
-    uint8_t *stg0 = epi + q * (2 * EPI_ROWS * 128);
+    const int ew = warp - 2;  // epilogue warp index
+    // Columns [ccol0, ccol0 + EPI_COLS_PER_WARP) of each tile are this warp's.
+    const int ccol0 = (ew >> 2) * Cfg::EPI_COLS_PER_WARP;
+    constexpr int EB = Cfg::EPI_BUFS;
+    uint8_t *stg0 = epi + ew * (EB * EPI_ROWS * 128);
     const uint32_t tempty_leader =
         (PAIR == 2) ? ptx::mapa(ptx::smem_u32(&tempty[0]), 0u) : ptx::smem_u32(&tempty[0]);
     const float alpha = p.alpha, beta = p.beta;
@@ -727,7 +742,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int prow = ptm * Cfg::UMMA_M + static_cast<int>(rank) * CTA_M + EPI_ROWS * q;
       if (prow >= p.M) return;
 #pragma unroll 1
-      for (int c = 0; c < BN / EPI_COLS; ++c) {
+      for (int c = ccol0 / EPI_COLS; c < (ccol0 + Cfg::EPI_COLS_PER_WARP) / EPI_COLS; ++c) {
         const int pcol = ptn * BN + c * EPI_COLS;
         if (pcol < p.N) ptx::tma_prefetch_l2_2d(&tmC, pcol, prow);
       }
@@ -785,7 +800,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t prow = part + static_cast<uint32_t>(r_loc) * (BN * 4);
         const uint32_t rsw = static_cast<uint32_t>(r_loc & 7);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
+        for (int c = ccol0 / 32; c < (ccol0 + Cfg::EPI_COLS_PER_WARP) / 32; c += 2) {
           uint32_t v[64];
           ptx::tmem_ld_32x32b_x32(tbase + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
           ptx::tmem_ld_32x32b_x32(tbase + 32 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
@@ -816,16 +831,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         //     rounds once to half and TMA-stores the chunk. Reads are coalesced: lanes
         //     16h..16h+15 take one row's 64 columns (256 contiguous bytes), so a warp load
         //     covers two rows; lane l holds rows 2i + l/16 (i < 16), columns 4(l%16)..+3.
-        const int workers = 4 * ksplit;
+        const int workers = Cfg::EPI_WARPS * ksplit;
         const int lhalf = lane >> 4, lg = lane & 15;
 #pragma unroll 1
-        for (int ci = 4 * split + q; okr && ci < 4 * (BN / 64); ci += workers) {
+        for (int ci = Cfg::EPI_WARPS * split + ew; okr && ci < 4 * (BN / 64); ci += workers) {
           const int rb = ci & 3, cb = ci >> 2;
           float f[64];
 #pragma unroll 1
           for (int t = 0; t < ksplit; ++t) {
             const uint32_t tb = (t == split) ? part : ptx::mapa(part, static_cast<uint32_t>(t));
-#pragma unroll
+#pragma unroll 8
             for (int i = 0; i < 16; ++i) {
               const int rr = 32 * rb + 2 * i + lhalf;
               const uint32_t g = static_cast<uint32_t>(16 * cb + lg);
@@ -858,9 +873,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               }
             }
           }
-          uint8_t *stg = stg0 + (chunk_ctr & 1) * (EPI_ROWS * 128);
+          uint8_t *stg = stg0 + (chunk_ctr % EB) * (EPI_ROWS * 128);
           ++chunk_ctr;
-          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          if (lane == 0) ptx::bulk_wait_group_read<EB - 1>();
           __syncwarp();
           // staging layout of the TMA store: row r's 16-byte group j at r*128 + (j ^ (r&7))*16;
           // this lane's 4 halves are the (lg&1) half of group lg/2.
@@ -984,16 +999,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool aborted_chunks = false;
       constexpr int NCH = BN / EPI_COLS;
       const bool unit_alpha = (alpha == 1.0f);
-      // The TMEM loads run one chunk ahead of the conversion and the stores (tcgen05.wait::ld
-      // waits for every load issued before it, so the next chunk's loads go out only after
-      // this chunk's registers were consumed).
-      uint32_t v[64];
-      auto load_chunk = [&](int c) {
-        ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
-                                *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-      };
-      load_chunk(0);
+      const int cbeg = ccol0 / EPI_COLS, cend = (ccol0 + Cfg::EPI_COLS_PER_WARP) / EPI_COLS;
       // beta != 0 with TMA stores: C_in is read with coalesced 16-byte loads (lane l takes
       // row 4i + l/8, 16-byte group l%8), one chunk ahead, and transposed through the
       // staging buffer so that each lane gets its own row.
@@ -1010,28 +1016,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             cin[i] = make_uint4(0u, 0u, 0u, 0u);
         }
       };
-      if (c_in) load_c(0);
+      if (c_in) load_c(cbeg);
 #pragma unroll 1
-      for (int c = 0; c < NCH; ++c, ++chunk_ctr) {
-        if (ACC_BUFS == 1 && c == NCH / 2) {
-          // Half 1 is announced separately; its first chunk could not be loaded ahead.
-          if (!wait_half1()) {
-            aborted_chunks = true;
-            break;
-          }
-          load_chunk(c);
+      for (int c = cbeg; c < cend; ++c, ++chunk_ctr) {
+        if (ACC_BUFS == 1 && c == NCH / 2 && !wait_half1()) {  // half 1 is announced separately
+          aborted_chunks = true;
+          break;
         }
-        ptx::tmem_ld_wait();
         float f[64];
-        if (unit_alpha) {
+        {
+          uint32_t v[64];
+          ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+          ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
+                                  *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+          ptx::tmem_ld_wait();
+          if (unit_alpha) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i]);
-        } else {
+            for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(v[i]);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) f[i] = alpha * __uint_as_float(v[i]);
+            for (int i = 0; i < 64; ++i) f[i] = alpha * __uint_as_float(v[i]);
+          }
         }
         const bool last_of_half = (ACC_BUFS == 1) && (c == NCH / 2 - 1);
-        if (c == NCH - 1 || last_of_half) {
+        if (c == cend - 1 || last_of_half) {
           // Accumulator (or, with one accumulator, one N half of it) fully read: hand it
           // back to the UMMA issuer.
           ptx::tc_fence_before();
@@ -1044,22 +1052,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             else
               ptx::mbar_arrive(tb);
           }
-        } else {
-          load_chunk(c + 1);
         }
         const int ccol = col0 + c * EPI_COLS;
-        uint8_t *stg = stg0 + (chunk_ctr & 1) * (EPI_ROWS * 128);
+        uint8_t *stg = stg0 + (chunk_ctr % EB) * (EPI_ROWS * 128);
 
         if (TMA_EPI) {
-          // The TMA store that used this staging buffer two chunks ago must have read it.
-          if (lane == 0) ptx::bulk_wait_group_read<1>();
+          // The TMA store that used this staging buffer EB chunks ago must have read it.
+          if (lane == 0) ptx::bulk_wait_group_read<EB - 1>();
           __syncwarp();
           if (c_in) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               *reinterpret_cast<uint4 *>(stg + sw128_off(4 * i + (lane >> 3), lane & 7)) = cin[i];
             __syncwarp();
-            if (c + 1 < NCH) load_c(c + 1);
+            if (c + 1 < cend) load_c(c + 1);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               // N % 8 == 0: a 16-byte group is wholly inside or outside C (zeros outside)
@@ -1348,16 +1354,16 @@ enum TileId {
   kNumTiles = 6
 };
 struct TileInfo {
-  int pair, bn, stages, smem, acc_bufs;
+  int pair, bn, stages, smem, acc_bufs, threads;
 };
+#define HGEMM_TILE_INFO(P, N)                                                              \
+  {P, N, TileCfg<P, N>::STAGES, TileCfg<P, N>::SMEM, TileCfg<P, N>::ACC_BUFS,              \
+   TileCfg<P, N>::THREADS}
 constexpr TileInfo kTiles[kNumTiles] = {
-    {2, 512, TileCfg<2, 512>::STAGES, TileCfg<2, 512>::SMEM, TileCfg<2, 512>::ACC_BUFS},
-    {2, 256, TileCfg<2, 256>::STAGES, TileCfg<2, 256>::SMEM, TileCfg<2, 256>::ACC_BUFS},
-    {2, 128, TileCfg<2, 128>::STAGES, TileCfg<2, 128>::SMEM, TileCfg<2, 128>::ACC_BUFS},
-    {1, 256, TileCfg<1, 256>::STAGES, TileCfg<1, 256>::SMEM, TileCfg<1, 256>::ACC_BUFS},
-    {1, 128, TileCfg<1, 128>::STAGES, TileCfg<1, 128>::SMEM, TileCfg<1, 128>::ACC_BUFS},
-    {1, 64, TileCfg<1, 64>::STAGES, TileCfg<1, 64>::SMEM, TileCfg<1, 64>::ACC_BUFS},
+    HGEMM_TILE_INFO(2, 512), HGEMM_TILE_INFO(2, 256), HGEMM_TILE_INFO(2, 128),
+    HGEMM_TILE_INFO(1, 256), HGEMM_TILE_INFO(1, 128), HGEMM_TILE_INFO(1, 64),
 };
+#undef HGEMM_TILE_INFO
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, KParams, PeerMaps);
 
@@ -1415,7 +1421,7 @@ int ensure_device(int dev, DevState **out) {
         d.attr_done[kT256x256][1] = true;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * d.pair_slots, 1, 1);
-        cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+        cfg.blockDim = dim3(kTiles[kT256x256].threads, 1, 1);
         cfg.dynamicSmemBytes = kTiles[kT256x256].smem;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1685,7 +1691,7 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid_ctas, 1, 1);
-  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.blockDim = dim3(ti.threads, 1, 1);
   cfg.dynamicSmemBytes = ti.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1784,6 +1790,16 @@ int hgemm_launch_ex(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *
   return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
                                 reinterpret_cast<cudaStream_t>(stream), force_bm, force_bn,
                                 group_m));
+}
+
+// GEMM without split-K for the multi-GPU layer (not part of the public header): its row
+// chunks must sum every element in the order the unsplit full-size GEMM does.
+__attribute__((visibility("hidden"))) int hgemm_internal_launch_unsplit(
+    const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
+    float alpha, float beta, hgemm_stream_t stream, int sm_limit) {
+  return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
+                                reinterpret_cast<cudaStream_t>(stream), 0, 0, 0,
+                                sm_limit > 0 ? sm_limit : 0, nullptr, 0, 1));
 }
 
 // Used by the multi-GPU layer only (not part of the public header).
