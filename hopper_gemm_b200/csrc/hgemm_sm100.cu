@@ -99,9 +99,12 @@ struct TileCfg {
   static constexpr int TX_BYTES = STAGE_BYTES * PAIR;        // armed on the leader's barrier
   // Epilogue warps: 8 for the 128- and 256-column tiles (two per TMEM lane quarter, each
   // taking half of the columns, so one warp's store waits overlap the other's conversions),
-  // 4 for the others. Staging: 32 KB either way (4 warps x 2 buffers or 8 x 1 of 4 KB).
+  // 4 for the others. Each warp double-buffers its 4 KB staging so that a chunk's
+  // conversion does not wait for the previous chunk's TMA store to read shared memory
+  // (thin-K on B200: +6..12% for 64 KB of staging, one pipeline stage fewer; large K
+  // unchanged).
   static constexpr int EPI_WARPS = (BN == 128 || BN == 256) ? HGEMM_EPI_WARPS_WIDE : 4;
-  static constexpr int EPI_BUFS = 8 / EPI_WARPS;
+  static constexpr int EPI_BUFS = 2;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int EPI_COLS_PER_WARP = BN * 4 / EPI_WARPS;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_ROWS * 128;
