@@ -1512,6 +1512,11 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
                           {kT256x128, 1.00, 1500.0}, {kT128x256, 1.05, 1500.0},
                           {kT128x128, 1.05, 1500.0}};
     const double kb = std::ceil(static_cast<double>(K) / BK);
+    // A pair tile also hands every tile index and stage across its two CTAs. With one or
+    // two k-blocks per tile (K <= 128) that costs more than the pair saves (B200, K = 128:
+    // 4096x8192 0.77 -> 0.83 of cuBLAS on 128x256, 16384x8192 0.88 -> 0.98); from K = 256
+    // the pair is faster again.
+    const double pair_extra = kb <= 2 ? 3000.0 : 0.0;
     double best = -1.0;
     for (const Cand &c : cands) {
       const TileInfo &ti = kTiles[c.tile];
@@ -1519,7 +1524,7 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
           static_cast<double>(ceil_div(M, CTA_M * ti.pair)) * ceil_div(N, ti.bn);
       const double slots = ti.pair == 2 ? pair_slots : sm_count;
       const double kb_time = std::max(4.0 * ti.bn / 2.0, 320.0);
-      const double tile_time = kb * kb_time + c.tile_cost;
+      const double tile_time = kb * kb_time + c.tile_cost + (ti.pair == 2 ? pair_extra : 0.0);
       const double makespan = tiles <= slots ? 1.0 : tiles / slots + 0.5;
       const double cost = makespan * tile_time * c.factor;
       if (best < 0 || cost < best) {
