@@ -29,7 +29,8 @@ class HgemmPlan(ctypes.Structure):
                 ("tiles_m", ctypes.c_int), ("tiles_n", ctypes.c_int),
                 ("grid_ctas", ctypes.c_int), ("pad_a", ctypes.c_int), ("pad_b", ctypes.c_int),
                 ("lda", ctypes.c_int), ("ldb", ctypes.c_int), ("tma_store", ctypes.c_int),
-                ("scratch_bytes", ctypes.c_size_t), ("sched_static", ctypes.c_int), ("ksplit", ctypes.c_int)]
+                ("scratch_bytes", ctypes.c_size_t), ("sched_static", ctypes.c_int), ("ksplit", ctypes.c_int),
+                ("epi_warps", ctypes.c_int)]
 
     def as_dict(self):
         return {name: getattr(self, name) for name, _ in self._fields_}

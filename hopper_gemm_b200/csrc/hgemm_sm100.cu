@@ -82,10 +82,7 @@ enum WaitSite : unsigned {
 };
 __device__ unsigned int g_dev_status = 0;
 
-#ifndef HGEMM_EPI_WARPS_WIDE
-#define HGEMM_EPI_WARPS_WIDE 8
-#endif
-template <int PAIR, int BN>
+template <int PAIR, int BN, int EPIW = 4>
 struct TileCfg {
   static constexpr int UMMA_N = BN < 256 ? BN : 256;        // N of one tcgen05.mma
   static constexpr int N_SUB = BN / UMMA_N;                  // UMMAs per k16 step
@@ -97,13 +94,12 @@ struct TileCfg {
   static constexpr int B_BYTES = B_COLS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TX_BYTES = STAGE_BYTES * PAIR;        // armed on the leader's barrier
-  // Epilogue warps: 8 for the 128- and 256-column tiles (two per TMEM lane quarter, each
-  // taking half of the columns, so one warp's store waits overlap the other's conversions),
-  // 4 for the others. Each warp double-buffers its 4 KB staging so that a chunk's
-  // conversion does not wait for the previous chunk's TMA store to read shared memory
-  // (thin-K on B200: +6..12% for 64 KB of staging, one pipeline stage fewer; large K
-  // unchanged).
-  static constexpr int EPI_WARPS = (BN == 128 || BN == 256) ? HGEMM_EPI_WARPS_WIDE : 4;
+  // Epilogue warps (EPIW): 4, one per TMEM lane quarter, or 8, two per quarter, each taking
+  // half of the columns (for the one-accumulator 256x512 tile each group of four drains
+  // one N half, so both halves drain at once). Each warp double-buffers a 4 KB staging
+  // buffer, so 8 warps cost 32 KB of pipeline stages; the planner uses them where the
+  // epilogue, not the main loop, sets the pace (see choose_epi_warps).
+  static constexpr int EPI_WARPS = EPIW;
   static constexpr int EPI_BUFS = 2;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int EPI_COLS_PER_WARP = BN * 4 / EPI_WARPS;
@@ -235,13 +231,17 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int j) {
 // one clock under the power cap). The leader CTA's producer thread owns that sequence and
 // publishes every tile index through a small shared-memory ring that the other roles of
 // both CTAs read; -1 ends the sequence.
-template <int PAIR, int BN, bool TMA_EPI>
-__global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
+template <int PAIR, int BN, bool TMA_EPI, int EPIW, bool SPLITK, bool PEERS>
+__global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
     hgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const KParams p,
                     const __grid_constant__ PeerMaps peers) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
-  using Cfg = TileCfg<PAIR, BN>;
+  using Cfg = TileCfg<PAIR, BN, EPIW>;
+  // Peer copies of every tile (fused multi-GPU path) exist only in the PEERS instances: the
+  // code alone cost the plain GEMM 1-6% (register pressure in the epilogue).
+  const int npeer = PEERS ? peers.n : 0;
+  static_assert(!SPLITK || (PAIR == 1 && TMA_EPI), "split-K: one-CTA tiles with TMA stores");
   constexpr int S = Cfg::STAGES;
   constexpr int NSL = Cfg::SCHED_SLOTS;
   constexpr int ACC_BUFS = Cfg::ACC_BUFS;
@@ -274,13 +274,16 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = (PAIR == 2) ? ptx::cluster_ctarank() : 0u;
-  // Split-K (one-CTA tiles): the cluster's CTAs share one tile, CTA `split` taking k-blocks
-  // [kb_begin, kb_end).
-  const int ksplit = (PAIR == 1 && p.ksplit > 1) ? p.ksplit : 1;
-  const int split = ksplit > 1 ? static_cast<int>(ptx::cluster_ctarank()) : 0;
-  const int kb_begin = static_cast<int>(static_cast<long long>(p.num_kb) * split / ksplit);
-  const int kb_end = static_cast<int>(static_cast<long long>(p.num_kb) * (split + 1) / ksplit);
-  const bool clustered = PAIR == 2 || ksplit > 1;
+  // Split-K (SPLITK instances only): the cluster's CTAs share one tile, CTA `split` taking
+  // k-blocks [kb_begin, kb_end).
+  const int ksplit = SPLITK ? p.ksplit : 1;
+  const int split = SPLITK ? static_cast<int>(ptx::cluster_ctarank()) : 0;
+  const int kb_begin =
+      SPLITK ? static_cast<int>(static_cast<long long>(p.num_kb) * split / ksplit) : 0;
+  const int kb_end =
+      SPLITK ? static_cast<int>(static_cast<long long>(p.num_kb) * (split + 1) / ksplit)
+             : p.num_kb;
+  constexpr bool clustered = PAIR == 2 || SPLITK;
   const int first_tile =
       clustered ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
 
@@ -291,7 +294,9 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(ptx::smem_u32(&tfull[a]), 1);
-      ptx::mbar_init(ptx::smem_u32(&tempty[a]), Cfg::EPI_WARPS * PAIR);
+      // One accumulator (BN = 512): each N half is drained by 4 warps per CTA (all 4 warps
+      // drain both halves, or with 8 warps each group of 4 drains one half).
+      ptx::mbar_init(ptx::smem_u32(&tempty[a]), (ACC_BUFS == 1 ? 4 : Cfg::EPI_WARPS) * PAIR);
     }
     ptx::mbar_init(ptx::smem_u32(drain), 1);
     // Readers of each tile index: leader MMA + the epilogue warps (+ the peer's producer and
@@ -313,7 +318,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
     ptx::prefetch_tmap(&tmB);
     if (TMA_EPI) {
       ptx::prefetch_tmap(&tmC);
-      for (int d = 0; d < peers.n; ++d) ptx::prefetch_tmap(&peers.m[d]);
+      for (int d = 0; d < npeer; ++d) ptx::prefetch_tmap(&peers.m[d]);
     }
   }
   if (warp == 1) {
@@ -729,7 +734,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
         const uint4 v = *reinterpret_cast<const uint4 *>(stgp + sw128_off(rr, jj));
         if (gr < p.M && gc < p.N) {
           const size_t off = static_cast<size_t>(gr) * p.N + gc;
-          for (int d = 0; d < peers.n; ++d) {
+          for (int d = 0; d < npeer; ++d) {
             if (p.c_evict_first)
               ptx::st_global_v4_hint(peers.ptr[d] + off, v, c_policy);
             else
@@ -793,7 +798,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
         if (okk) ptx::tc_fence_after();
         return okk != 0;
       };
-      if (PAIR == 1 && TMA_EPI && ksplit > 1) {
+      if constexpr (SPLITK) {
         // ---- split-K: one tile per cluster, CTA `split` holds the sums of its k-blocks.
         // (1) partial sums -> this CTA's shared memory, fp32 (the pipeline stages are free:
         //     every UMMA of the cluster's only tile has retired). Row r (tile-local) starts
@@ -914,7 +919,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
         ++it;
         continue;
       }
-      if constexpr (ACC_BUFS == 1 && TMA_EPI) {
+      if constexpr (ACC_BUFS == 1 && TMA_EPI && Cfg::EPI_WARPS == 4) {
         if (beta == 0.0f) {
           // Single accumulator: drain each N half into registers as packed halves, give that
           // half of TMEM back at once, then store it through the swizzled staging buffers
@@ -986,12 +991,12 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
                 if (row0 < p.M && ccol < p.N) {
                   store_c(&tmC, ptx::smem_u32(stg0) + buf, ccol, row0);
                   if (!peers.lsu)
-                    for (int d = 0; d < peers.n; ++d)
+                    for (int d = 0; d < npeer; ++d)
                       store_c(&peers.m[d], ptx::smem_u32(stg0) + buf, ccol, row0);
                 }
                 ptx::bulk_commit_group();
               }
-              if (peers.n > 0 && peers.lsu) push_peers(stg0 + buf, row0, ccol);
+              if (npeer > 0 && peers.lsu) push_peers(stg0 + buf, row0, ccol);
             }
           }
           if (aborted) break;
@@ -1020,14 +1025,41 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
         }
       };
       if (c_in) load_c(cbeg);
+      // With 4 warps (255 registers each) the TMEM loads run one chunk ahead of the
+      // conversion and the stores; tcgen05.wait::ld waits for every load issued before it,
+      // so the next chunk's loads go out only after this chunk's words were consumed. The
+      // 8-warp flavours (168 registers) load each chunk when they reach it.
+      constexpr bool kPipe = Cfg::EPI_WARPS == 4;
+      uint32_t vn[kPipe ? 64 : 1];
+      auto issue_ld = [&](int c) {
+        if constexpr (kPipe) {
+          ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS, *reinterpret_cast<uint32_t(*)[32]>(&vn[0]));
+          ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
+                                  *reinterpret_cast<uint32_t(*)[32]>(&vn[32]));
+        }
+      };
+      if (!(ACC_BUFS == 1 && cbeg == NCH / 2)) issue_ld(cbeg);
 #pragma unroll 1
       for (int c = cbeg; c < cend; ++c, ++chunk_ctr) {
-        if (ACC_BUFS == 1 && c == NCH / 2 && !wait_half1()) {  // half 1 is announced separately
-          aborted_chunks = true;
-          break;
+        if (ACC_BUFS == 1 && c == NCH / 2) {  // half 1 is announced separately
+          if (!wait_half1()) {
+            aborted_chunks = true;
+            break;
+          }
+          issue_ld(c);  // (its first chunk could not be loaded ahead)
         }
         float f[64];
-        {
+        if constexpr (kPipe) {
+          ptx::tmem_ld_wait();
+          if (unit_alpha) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) f[i] = __uint_as_float(vn[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) f[i] = alpha * __uint_as_float(vn[i]);
+          }
+          if (c + 1 < cend && !(ACC_BUFS == 1 && c + 1 == NCH / 2)) issue_ld(c + 1);
+        } else {
           uint32_t v[64];
           ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
           ptx::tmem_ld_32x32b_x32(tbase + c * EPI_COLS + 32,
@@ -1097,12 +1129,12 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
             if (row0 < p.M && ccol < p.N) {
               store_c(&tmC, ptx::smem_u32(stg), ccol, row0);
               if (!peers.lsu)
-                for (int d = 0; d < peers.n; ++d)
+                for (int d = 0; d < npeer; ++d)
                   store_c(&peers.m[d], ptx::smem_u32(stg), ccol, row0);
             }
             ptx::bulk_commit_group();  // one group per chunk, empty when nothing was stored
           }
-          if (peers.n > 0 && peers.lsu) push_peers(stg, row0, ccol);
+          if (npeer > 0 && peers.lsu) push_peers(stg, row0, ccol);
         } else {
           // C's rows are not 16-byte aligned: stage through smem, then coalesced 2-byte
           // accesses (lanes along a row), predicated on the M/N edges.
@@ -1163,7 +1195,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN>::THREADS, 1)
     }
     if (TMA_EPI && lane == 0) ptx::bulk_wait_group<0>();
     // Stores into peers' memory: complete and ordered system-wide before the CTA exits.
-    if (peers.n > 0) __threadfence_system();
+    if (npeer > 0) __threadfence_system();
     __syncwarp();
   }
 
@@ -1356,28 +1388,68 @@ enum TileId {
   kT128x64 = 5,
   kNumTiles = 6
 };
+// Kernel flavours of one tile: TMA-store epilogue with 4 or 8 warps, the SIMT-store epilogue
+// (N % 8 != 0, 4 warps), split-K (one-CTA tiles, TMA stores, 4 warps), and the peer-copy
+// epilogues of the fused multi-GPU path (256x512 and 256x256 only). An 8-warp flavour that
+// is not instantiated (128x64) maps to the 4-warp one; a missing split-K or peer flavour is
+// reported by kernel_for returning nullptr.
+enum Flavor {
+  kFlavE4 = 0,
+  kFlavE8 = 1,
+  kFlavSimt = 2,
+  kFlavSplit = 3,
+  kFlavPeerE4 = 4,  // TMA-store epilogues that also copy every tile to peer buffers
+  kFlavPeerE8 = 5,
+  kNumFlavors = 6
+};
+struct FlavorInfo {
+  int stages, smem, threads, epi_warps;
+};
 struct TileInfo {
-  int pair, bn, stages, smem, acc_bufs, threads;
+  int pair, bn, acc_bufs;
+  FlavorInfo flav[kNumFlavors];
 };
-#define HGEMM_TILE_INFO(P, N)                                                              \
-  {P, N, TileCfg<P, N>::STAGES, TileCfg<P, N>::SMEM, TileCfg<P, N>::ACC_BUFS,              \
-   TileCfg<P, N>::THREADS}
+#define HGEMM_FLAV(P, N, E)                                                                  \
+  { TileCfg<P, N, E>::STAGES, TileCfg<P, N, E>::SMEM, TileCfg<P, N, E>::THREADS, E }
+#define HGEMM_TILE(P, N, E4T, E8T)                                                           \
+  {P, N, TileCfg<P, N>::ACC_BUFS,                                                            \
+   {HGEMM_FLAV(P, N, E4T), HGEMM_FLAV(P, N, E8T), HGEMM_FLAV(P, N, 4), HGEMM_FLAV(P, N, 4),  \
+    HGEMM_FLAV(P, N, E4T), HGEMM_FLAV(P, N, E8T)}}
 constexpr TileInfo kTiles[kNumTiles] = {
-    HGEMM_TILE_INFO(2, 512), HGEMM_TILE_INFO(2, 256), HGEMM_TILE_INFO(2, 128),
-    HGEMM_TILE_INFO(1, 256), HGEMM_TILE_INFO(1, 128), HGEMM_TILE_INFO(1, 64),
+    HGEMM_TILE(2, 512, 4, 8), HGEMM_TILE(2, 256, 4, 8), HGEMM_TILE(2, 128, 4, 8),
+    HGEMM_TILE(1, 256, 4, 8), HGEMM_TILE(1, 128, 4, 8), HGEMM_TILE(1, 64, 4, 4),
 };
-#undef HGEMM_TILE_INFO
+#undef HGEMM_TILE
+#undef HGEMM_FLAV
 
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, KParams, PeerMaps);
 
-KernelFn kernel_for(int tile, bool tma_epi) {
+template <int P, int N, int E4T, int E8T, bool HAS_SPLIT, bool HAS_PEERS>
+KernelFn flavor_kernel(int flavor) {
+  switch (flavor) {
+    case kFlavE8: return hgemm_tc_kernel<P, N, true, E8T, false, false>;
+    case kFlavSimt: return hgemm_tc_kernel<P, N, false, 4, false, false>;
+    case kFlavSplit:
+      if constexpr (HAS_SPLIT) return hgemm_tc_kernel<P, N, true, 4, true, false>;
+      return nullptr;
+    case kFlavPeerE4:
+      if constexpr (HAS_PEERS) return hgemm_tc_kernel<P, N, true, E4T, false, true>;
+      return nullptr;
+    case kFlavPeerE8:
+      if constexpr (HAS_PEERS) return hgemm_tc_kernel<P, N, true, E8T, false, true>;
+      return nullptr;
+    default: return hgemm_tc_kernel<P, N, true, E4T, false, false>;
+  }
+}
+
+KernelFn kernel_for(int tile, int flavor) {
   switch (tile) {
-    case kT256x512: return tma_epi ? hgemm_tc_kernel<2, 512, true> : hgemm_tc_kernel<2, 512, false>;
-    case kT256x256: return tma_epi ? hgemm_tc_kernel<2, 256, true> : hgemm_tc_kernel<2, 256, false>;
-    case kT256x128: return tma_epi ? hgemm_tc_kernel<2, 128, true> : hgemm_tc_kernel<2, 128, false>;
-    case kT128x256: return tma_epi ? hgemm_tc_kernel<1, 256, true> : hgemm_tc_kernel<1, 256, false>;
-    case kT128x128: return tma_epi ? hgemm_tc_kernel<1, 128, true> : hgemm_tc_kernel<1, 128, false>;
-    default: return tma_epi ? hgemm_tc_kernel<1, 64, true> : hgemm_tc_kernel<1, 64, false>;
+    case kT256x512: return flavor_kernel<2, 512, 4, 8, false, true>(flavor);
+    case kT256x256: return flavor_kernel<2, 256, 4, 8, false, true>(flavor);
+    case kT256x128: return flavor_kernel<2, 128, 4, 8, false, false>(flavor);
+    case kT128x256: return flavor_kernel<1, 256, 4, 8, true, false>(flavor);
+    case kT128x128: return flavor_kernel<1, 128, 4, 8, true, false>(flavor);
+    default: return flavor_kernel<1, 64, 4, 4, true, false>(flavor);
   }
 }
 
@@ -1393,7 +1465,7 @@ struct DevState {
   int sm_count = 148;
   int cc_major = 0, cc_minor = 0;
   int pair_slots = 74;        // co-resident 2-CTA clusters at our shared-memory size
-  bool attr_done[kNumTiles][2] = {};
+  bool attr_done[kNumTiles][kNumFlavors] = {};
   void *scratch = nullptr;
   size_t scratch_bytes = 0;
 };
@@ -1418,14 +1490,15 @@ int ensure_device(int dev, DevState **out) {
     d.init = true;
     if (d.cc_major == 10 && d.cc_minor == 0) {
       // Co-resident clusters of two at this shared-memory size (GPC pairing may leave SMs out).
-      KernelFn k = kernel_for(kT256x256, true);
-      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kTiles[kT256x256].smem) == cudaSuccess) {
-        d.attr_done[kT256x256][1] = true;
+      const FlavorInfo &fi = kTiles[kT256x256].flav[kFlavE4];
+      KernelFn k = kernel_for(kT256x256, kFlavE4);
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, fi.smem) ==
+          cudaSuccess) {
+        d.attr_done[kT256x256][kFlavE4] = true;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * d.pair_slots, 1, 1);
-        cfg.blockDim = dim3(kTiles[kT256x256].threads, 1, 1);
-        cfg.dynamicSmemBytes = kTiles[kT256x256].smem;
+        cfg.blockDim = dim3(fi.threads, 1, 1);
+        cfg.dynamicSmemBytes = fi.smem;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
@@ -1452,6 +1525,15 @@ int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b
 // critical path (waves x columns per CTA), preferring the pair tiles, whose A+B traffic per
 // flop is the lowest. group_m keeps the concurrently running tiles' A and B blocks small
 // enough to stay in the 126 MB L2.
+// Epilogue width of a tile's TMA-store flavour. 8 warps pay only where the epilogue sets the
+// pace, tiles of at most 2 k-blocks (K <= 128: 4096x8192x128 0.78 -> 0.91 of cuBLAS,
+// 16384x8192x128 0.89 -> 1.00 on B200); from K = 256 the 32 KB of pipeline stages they cost
+// weigh more (4096x8192x256 on 256x256: 0.85 with 4 warps, 0.80 with 8).
+int choose_epi_warps(int tile, int kbn) {
+  if (tile == kT128x64) return 4;
+  return kbn <= 2 ? 8 : 4;
+}
+
 int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int force_bn,
               int group_m, int sm_count, int pair_slots, hgemm_plan_t *pl,
               bool persistent_only = false, int ksplit_req = 0) {
@@ -1537,7 +1619,13 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   pl->pair = ti.pair;
   pl->tile_m = CTA_M * ti.pair;
   pl->tile_n = ti.bn;
-  pl->stages = ti.stages;
+  {
+    const int kbn0 = ceil_div(K, BK);
+    const int flav = !pl->tma_store ? kFlavSimt
+                     : (choose_epi_warps(tile, kbn0) == 8 ? kFlavE8 : kFlavE4);
+    pl->stages = ti.flav[flav].stages;
+    pl->epi_warps = ti.flav[flav].epi_warps;
+  }
   pl->tiles_m = ceil_div(M, pl->tile_m);
   pl->tiles_n = ceil_div(N, pl->tile_n);
   const long long total = static_cast<long long>(pl->tiles_m) * pl->tiles_n;
@@ -1588,7 +1676,8 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
     pl->pair = 1;
     pl->tile_m = CTA_M;
     pl->tile_n = st.bn;
-    pl->stages = st.stages;
+    pl->stages = st.flav[kFlavSplit].stages;
+    pl->epi_warps = st.flav[kFlavSplit].epi_warps;
     pl->tiles_m = ceil_div(M, CTA_M);
     pl->tiles_n = ceil_div(N, st.bn);
     pl->ksplit = ks;
@@ -1670,14 +1759,20 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
     peers.n = npeers;
     peers.lsu = HGEMM_PEER_PUSH_LSU;
   }
-  KernelFn k = kernel_for(tile, tma_epi);
-  if (!d.attr_done[tile][tma_epi]) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, ti.smem) !=
+  const int flav = !tma_epi ? kFlavSimt
+                   : pl.ksplit > 1 ? kFlavSplit
+                   : npeers > 0 ? (pl.epi_warps == 8 ? kFlavPeerE8 : kFlavPeerE4)
+                   : (pl.epi_warps == 8 ? kFlavE8 : kFlavE4);
+  const FlavorInfo &fi = ti.flav[flav];
+  KernelFn k = kernel_for(tile, flav);
+  if (!k) return npeers > 0 ? HGEMM_ERR_NOT_FUSABLE : HGEMM_ERR_INVALID_ARG;
+  if (!d.attr_done[tile][flav]) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, fi.smem) !=
         cudaSuccess) {
       cudaGetLastError();
       return HGEMM_ERR_CUDA;
     }
-    d.attr_done[tile][tma_epi] = true;
+    d.attr_done[tile][flav] = true;
   }
   KParams kp;
   kp.M = M;
@@ -1699,8 +1794,8 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid_ctas, 1, 1);
-  cfg.blockDim = dim3(ti.threads, 1, 1);
-  cfg.dynamicSmemBytes = ti.smem;
+  cfg.blockDim = dim3(fi.threads, 1, 1);
+  cfg.dynamicSmemBytes = fi.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1744,11 +1839,12 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
   if (st != HGEMM_OK) return st;
   if (pl.path == 0) return HGEMM_OK;
   if (npeers > 0 && (pl.path != 1 || !pl.tma_store)) return HGEMM_ERR_NOT_FUSABLE;
-  if (npeers > 0 && force_bm == 0 && pl.tile_n == 512 && K < kPeerWideTileMinK) {
-    // Every tile's epilogue also stores to the peers. With the single 512-column
-    // accumulator that longer epilogue sits between tiles; the double-buffered 256x256 tile
-    // hides it behind the next tile's main loop (measured on 2 B200s: faster at K = 8192,
-    // slower at K = 16384).
+  if (npeers > 0 && force_bm == 0 &&
+      !(pl.pair == 2 && (pl.tile_n == 256 || (pl.tile_n == 512 && K >= kPeerWideTileMinK)))) {
+    // Every tile's epilogue also stores to the peers (peer flavours exist for 256x512 and
+    // 256x256 only). With the single 512-column accumulator that longer epilogue sits
+    // between tiles; the double-buffered 256x256 tile hides it behind the next tile's main
+    // loop (measured on 2 B200s: faster at K = 8192, slower at K = 16384).
     st = make_plan(M, N, K, beta, aligned16, 256, 256, group_m, sms, pslots, &pl, sm_limit > 0,
                    1);
     if (st != HGEMM_OK) return st;

@@ -169,6 +169,7 @@ typedef struct {
                             tiles co-resident); 0: cluster launch control */
   int ksplit;            /* > 1: split-K, a cluster of ksplit one-CTA tiles shares each tile's
                             k-blocks (grid_ctas = tiles * ksplit) */
+  int epi_warps;         /* epilogue warps per CTA: 4, or 8 where the epilogue sets the pace */
 } hgemm_plan_t;
 
 /* `aligned16` says whether A, B and C all start on 16-byte boundaries; `sm_count` and

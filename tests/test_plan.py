@@ -38,7 +38,7 @@ def test_large_square_uses_widest_pair_tile():
     # bytes per flop) is chosen
     p = hg.plan(8192, 8192, 8192, **B200)
     assert (p["tile_m"], p["tile_n"], p["pair"]) == (256, 512, 2)
-    assert p["grid_ctas"] == 2 * 32 * 16 and p["stages"] >= 4
+    assert p["grid_ctas"] == 2 * 32 * 16 and p["stages"] >= 3
     assert 1 <= p["group_m"] <= p["tiles_m"]
 
 
