@@ -196,7 +196,7 @@ def cpu_baseline(M, N, K, budget_s=10.0):
     orc.build()
     threads = orc.max_threads()
     B = orc.hash_fill_half((K, N), 0x85EBCA6B)
-    rows_probe = 4
+    rows_probe = max(4, threads)  # one row per thread, so the probe rate scales
     A = orc.hash_fill_half((rows_probe, K), 0x9E3779B9)
     t0 = time.perf_counter()
     orc.gemm_f64(A, B, rows=np.arange(rows_probe), threads=threads)
