@@ -1594,11 +1594,12 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
                           {kT256x128, 1.00, 1500.0}, {kT128x256, 1.05, 1500.0},
                           {kT128x128, 1.05, 1500.0}};
     const double kb = std::ceil(static_cast<double>(K) / BK);
-    // A pair tile also hands every tile index and stage across its two CTAs. With one or
-    // two k-blocks per tile (K <= 128) that costs more than the pair saves (B200, K = 128:
-    // 4096x8192 0.77 -> 0.83 of cuBLAS on 128x256, 16384x8192 0.88 -> 0.98); from K = 256
-    // the pair is faster again.
-    const double pair_extra = kb <= 2 ? 3000.0 : 0.0;
+    // A pair tile also hands every tile index and stage across its two CTAs. With at most
+    // four k-blocks per tile (K <= 256) that costs more than the pair saves (B200, one-CTA
+    // 128x256 against the 256x256 pair: K = 128 4096x8192 0.77 -> 0.83 of cuBLAS,
+    // 16384x8192 0.88 -> 0.98; K = 256 8192x8192 0.93 -> 0.96); from K = 512 the pair is
+    // faster.
+    const double pair_extra = kb <= 4 ? 3000.0 : 0.0;
     double best = -1.0;
     for (const Cand &c : cands) {
       const TileInfo &ti = kTiles[c.tile];
