@@ -1599,13 +1599,16 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
     // 128x256 against the 256x256 pair: K = 128 4096x8192 0.77 -> 0.83 of cuBLAS,
     // 16384x8192 0.88 -> 0.98; K = 256 8192x8192 0.93 -> 0.96); from K = 512 the pair is
     // faster.
-    const double pair_extra = kb <= 4 ? 3000.0 : 0.0;
+    // The same holds for a single wave of tiles with at most 8 k-blocks, where the pair's
+    // start-up hand-offs are not amortised (2048x2048x512: 0.70 -> 0.85 on 128x256).
     double best = -1.0;
     for (const Cand &c : cands) {
       const TileInfo &ti = kTiles[c.tile];
       const double tiles =
           static_cast<double>(ceil_div(M, CTA_M * ti.pair)) * ceil_div(N, ti.bn);
       const double slots = ti.pair == 2 ? pair_slots : sm_count;
+      const bool pair_slow = kb <= 4 || (kb <= 8 && tiles <= slots);
+      const double pair_extra = pair_slow ? 3000.0 : 0.0;
       const double kb_time = std::max(4.0 * ti.bn / 2.0, 320.0);
       const double tile_time = kb * kb_time + c.tile_cost + (ti.pair == 2 ? pair_extra : 0.0);
       const double makespan = tiles <= slots ? 1.0 : tiles / slots + 0.5;
