@@ -30,7 +30,7 @@ class HgemmPlan(ctypes.Structure):
                 ("grid_ctas", ctypes.c_int), ("pad_a", ctypes.c_int), ("pad_b", ctypes.c_int),
                 ("lda", ctypes.c_int), ("ldb", ctypes.c_int), ("tma_store", ctypes.c_int),
                 ("scratch_bytes", ctypes.c_size_t), ("sched_static", ctypes.c_int), ("ksplit", ctypes.c_int),
-                ("epi_warps", ctypes.c_int)]
+                ("epi_warps", ctypes.c_int), ("pad_c", ctypes.c_int), ("ldc", ctypes.c_int)]
 
     def as_dict(self):
         return {name: getattr(self, name) for name, _ in self._fields_}
@@ -79,7 +79,9 @@ def _load():
         raise ImportError(
             f"{LIB_PATH} is not built: run `python -c 'import __graft_entry__ as g; g.build()'` "
             "(nvcc, sm_100a). The GEMM has no CPU fallback.")
-    lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+    # RTLD_LOCAL: the library's exported names stay out of the global symbol scope, so
+    # they cannot interpose on another library that exports the same names.
+    lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_LOCAL)
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.restype = res

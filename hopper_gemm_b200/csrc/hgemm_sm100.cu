@@ -127,6 +127,7 @@ struct KParams {
   unsigned long long timeout_ns;
   int sched_static;  // 1: cluster c takes tiles c, c + clusters, ...; 0: cluster launch control
   int c_evict_first;  // 1: C stores (local and peer) are marked evict-first in L2
+  int ldc;            // row stride of C in halves (N, or N rounded up to 8 for the padded copy)
   int ksplit;         // > 1 (one-CTA tiles only): a cluster of ksplit CTAs shares each tile's
                       // k-blocks and reduces the partial sums over distributed shared memory
 };
@@ -869,9 +870,11 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               const int grow = tm * CTA_M + 32 * rb + 2 * i + lhalf;
-              if (grow < p.M && gcol < p.N) {  // N % 8 == 0: 4 halves wholly inside or outside
+              // ldc % 8 == 0: a group of 4 halves that starts inside a row ends inside its
+              // stride (pad columns of a restrided C hold zeros and are never stored)
+              if (grow < p.M && gcol < p.N) {
                 const uint2 u = __ldg(reinterpret_cast<const uint2 *>(
-                    p.C + static_cast<long long>(grow) * p.N + gcol));
+                    p.C + static_cast<long long>(grow) * p.ldc + gcol));
                 const float2 c0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
                 const float2 c1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
                 f[4 * i] = fmaf(beta, c0.x, f[4 * i]);
@@ -1019,7 +1022,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
         for (int i = 0; i < 8; ++i) {
           const int gr = row0 + 4 * i + (lane >> 3);
           if (gr < p.M && gc < p.N)
-            cin[i] = __ldg(reinterpret_cast<const uint4 *>(p.C + static_cast<long long>(gr) * p.N + gc));
+            cin[i] = __ldg(reinterpret_cast<const uint4 *>(p.C + static_cast<long long>(gr) * p.ldc + gc));
           else
             cin[i] = make_uint4(0u, 0u, 0u, 0u);
         }
@@ -1279,6 +1282,19 @@ __global__ void __launch_bounds__(256) restride_kernel(const __half *__restrict_
     for (int e = 0; e < 8; ++e) v[e] = (c + e < cols) ? s[c + e] : __float2half(0.0f);
     *reinterpret_cast<uint4 *>(dst + static_cast<long long>(r) * ld + c) =
         *reinterpret_cast<const uint4 *>(v);
+  }
+}
+
+// Inverse of restride_kernel: rows x cols out of a buffer with row stride `ld` into a
+// row-major rows x cols matrix. One element per thread step; consecutive lanes take
+// consecutive columns, so loads and stores are coalesced.
+__global__ void __launch_bounds__(256) compact_kernel(const __half *__restrict__ src,
+                                                      __half *__restrict__ dst, int rows,
+                                                      int cols, int ld) {
+  const long long total = static_cast<long long>(rows) * cols;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
+    const long long r = i / cols;
+    dst[i] = src[r * ld + (i - r * cols)];
   }
 }
 
@@ -1560,16 +1576,24 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
     pl->grid_ctas = pl->tiles_m * pl->tiles_n;
     return HGEMM_OK;
   }
-  (void)beta;
   pl->path = 1;
   pl->lda = (K + 7) & ~7;
   pl->ldb = (N + 7) & ~7;
   pl->pad_a = pl->lda != K;
   pl->pad_b = pl->ldb != N;
+  // C with N % 8 != 0 has rows that TMA cannot address. With beta != 0 the GEMM runs on a
+  // copy of C with a 16-byte row stride (restrided in, compacted back), two HBM-bound
+  // passes instead of an epilogue of 2-byte loads and stores (B200: 4095^3 beta = 0.5
+  // 374 -> 207 us, 8192x8191x8192 1634 -> 1032 us). With beta == 0 the compaction costs
+  // more than the 2-byte stores save (4095^3: 162 us direct, 185 us padded), so those
+  // shapes keep the SIMT-store epilogue.
+  pl->pad_c = (N % 8 != 0) && beta != 0.0f;
+  pl->ldc = pl->pad_c ? pl->ldb : N;
   pl->scratch_bytes = ((pl->pad_a ? static_cast<size_t>(M) * pl->lda : 0) +
-                       (pl->pad_b ? static_cast<size_t>(K) * pl->ldb : 0)) *
+                       (pl->pad_b ? static_cast<size_t>(K) * pl->ldb : 0) +
+                       (pl->pad_c ? static_cast<size_t>(M) * pl->ldc : 0)) *
                       sizeof(__half);
-  pl->tma_store = (N % 8 == 0) ? 1 : 0;
+  pl->tma_store = (N % 8 == 0 || pl->pad_c) ? 1 : 0;
 
   int tile = tile_from_force(force_bm, force_bn);
   if (tile < 0) {
@@ -1745,7 +1769,7 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   if (!encode_2d(&ta, A, M, K, lda, CTA_M, BK) || !encode_2d(&tb, B, K, N, ldb, BK, 64))
     return HGEMM_ERR_TENSOR_MAP;
   if (tma_epi) {
-    if (!encode_2d(&tc, C, M, N, N, EPI_ROWS, EPI_COLS)) return HGEMM_ERR_TENSOR_MAP;
+    if (!encode_2d(&tc, C, M, N, pl.ldc, EPI_ROWS, EPI_COLS)) return HGEMM_ERR_TENSOR_MAP;
   } else {
     tc = ta;
   }
@@ -1790,6 +1814,7 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   kp.alpha = alpha;
   kp.beta = beta;
   kp.C = C;
+  kp.ldc = pl.ldc;
   kp.timeout_ns = g_timeout_ns.load();
   kp.sched_static = pl.sched_static;
   kp.ksplit = pl.ksplit > 1 ? pl.ksplit : 1;
@@ -1813,6 +1838,52 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
     return HGEMM_ERR_LAUNCH;
   }
   return HGEMM_OK;
+}
+
+int launch_compact(const __half *src, __half *dst, int rows, int cols, int ld, int sm_count,
+                   cudaStream_t stream) {
+  const long long n = static_cast<long long>(rows) * cols;
+  const int blocks = static_cast<int>(std::min<long long>((n + 255) / 256, sm_count * 8LL));
+  compact_kernel<<<std::max(blocks, 1), 256, 0, stream>>>(src, dst, rows, cols, ld);
+  return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
+}
+
+// The tcgen05 path of a plan: restride A (K % 8 != 0) and B (N % 8 != 0) into scratch `w`,
+// run the GEMM (into a 16-byte-strided copy of C when N % 8 != 0, read in first when
+// beta != 0) and compact that copy back into C. `w` holds pl.scratch_bytes (A, then B, then
+// C); every element the GEMM reads from it is written earlier on the same stream.
+int launch_padded(const hgemm_plan_t &pl, const __half *A, const __half *B, __half *C, int M,
+                  int N, int K, float alpha, float beta, cudaStream_t stream, DevState &d,
+                  __half *w, __half *const *peer_C, int npeers) {
+  int st = HGEMM_OK;
+  const __half *Ause = A, *Buse = B;
+  __half *Cuse = C;
+  const size_t na = pl.pad_a ? static_cast<size_t>(M) * pl.lda : 0;
+  const size_t nb = pl.pad_b ? static_cast<size_t>(K) * pl.ldb : 0;
+  if (pl.pad_a) {
+    st = launch_restride(A, w, M, K, pl.lda, d.sm_count, stream);
+    if (st != HGEMM_OK) return st;
+    Ause = w;
+  }
+  if (pl.pad_b) {
+    st = launch_restride(B, w + na, K, N, pl.ldb, d.sm_count, stream);
+    if (st != HGEMM_OK) return st;
+    Buse = w + na;
+  }
+  if (pl.pad_c) {
+    Cuse = w + na + nb;
+    if (beta != 0.0f) {
+      st = launch_restride(C, Cuse, M, N, pl.ldc, d.sm_count, stream);
+      if (st != HGEMM_OK) return st;
+    }
+  }
+  int tile = -1;
+  for (int t = 0; t < kNumTiles; ++t)
+    if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;
+  st = launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, Cuse, M, N, K, alpha, beta, stream, d,
+                 peer_C, npeers);
+  if (st != HGEMM_OK || !pl.pad_c) return st;
+  return launch_compact(Cuse, C, M, N, pl.ldc, d.sm_count, stream);
 }
 
 int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K, float alpha,
@@ -1842,7 +1913,7 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
                  sm_limit > 0, npeers > 0 ? 1 : ksplit_req);
   if (st != HGEMM_OK) return st;
   if (pl.path == 0) return HGEMM_OK;
-  if (npeers > 0 && (pl.path != 1 || !pl.tma_store)) return HGEMM_ERR_NOT_FUSABLE;
+  if (npeers > 0 && (pl.path != 1 || !pl.tma_store || pl.pad_c)) return HGEMM_ERR_NOT_FUSABLE;
   if (npeers > 0 && force_bm == 0 &&
       !(pl.pair == 2 && (pl.tile_n == 256 || (pl.tile_n == 512 && K >= kPeerWideTileMinK)))) {
     // Every tile's epilogue also stores to the peers (peer flavours exist for 256x512 and
@@ -1855,27 +1926,12 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
   }
   if (pl.path == 2) return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
 
-  const __half *Ause = A, *Buse = B;
-  if (pl.pad_a || pl.pad_b) {
-    __half *w = static_cast<__half *>(scratch_get(*d, pl.scratch_bytes));
+  __half *w = nullptr;
+  if (pl.pad_a || pl.pad_b || pl.pad_c) {
+    w = static_cast<__half *>(scratch_get(*d, pl.scratch_bytes));
     if (!w) return HGEMM_ERR_ALLOC;
-    const size_t na = pl.pad_a ? static_cast<size_t>(M) * pl.lda : 0;
-    if (pl.pad_a) {
-      st = launch_restride(A, w, M, K, pl.lda, d->sm_count, stream);
-      if (st != HGEMM_OK) return st;
-      Ause = w;
-    }
-    if (pl.pad_b) {
-      st = launch_restride(B, w + na, K, N, pl.ldb, d->sm_count, stream);
-      if (st != HGEMM_OK) return st;
-      Buse = w + na;
-    }
   }
-  int tile = -1;
-  for (int t = 0; t < kNumTiles; ++t)
-    if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;
-  return launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, C, M, N, K, alpha, beta, stream, *d,
-                   peer_C, npeers);
+  return launch_padded(pl, A, B, C, M, N, K, alpha, beta, stream, *d, w, peer_C, npeers);
 }
 
 // ---------------------------------------------------------------- autotune cache
@@ -2203,33 +2259,19 @@ int launch_noalloc_impl(const __half *A, const __half *B, __half *C, int M, int 
   if (st != HGEMM_OK) return st;
   if (pl.path == 0) return HGEMM_OK;
   if (pl.path == 2) return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
-  const __half *Ause = A, *Buse = B;
-  if (pl.pad_a || pl.pad_b) {
+  __half *w = nullptr;
+  if (pl.pad_a || pl.pad_b || pl.pad_c) {
     if (pl.scratch_bytes > kNoallocScratchBytes) return HGEMM_ERR_TOO_LARGE;
-    __half *w = nullptr;
     {
       std::lock_guard<std::mutex> lk(g_noalloc_mu);
       st = noalloc_scratch(dev, &w);
     }
     if (st != HGEMM_OK) return st;
     // Nothing here has to start at zero: each element the GEMM reads from the array is
-    // written by the restride pass of this same call, earlier on the same stream.
-    const size_t na = pl.pad_a ? static_cast<size_t>(M) * pl.lda : 0;
-    if (pl.pad_a) {
-      st = launch_restride(A, w, M, K, pl.lda, d->sm_count, stream);
-      if (st != HGEMM_OK) return st;
-      Ause = w;
-    }
-    if (pl.pad_b) {
-      st = launch_restride(B, w + na, K, N, pl.ldb, d->sm_count, stream);
-      if (st != HGEMM_OK) return st;
-      Buse = w + na;
-    }
+    // written by the restride passes of this same call, earlier on the same stream (the C
+    // copy is only read when beta != 0, after C was restrided into it).
   }
-  int tile = -1;
-  for (int t = 0; t < kNumTiles; ++t)
-    if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;
-  return launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, C, M, N, K, alpha, beta, stream, *d);
+  return launch_padded(pl, A, B, C, M, N, K, alpha, beta, stream, *d, w, nullptr, 0);
 }
 
 }  // namespace

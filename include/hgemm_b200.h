@@ -163,13 +163,16 @@ typedef struct {
                      control); with sched_static == 1 one persistent cluster per slot */
   int pad_a, pad_b;      /* operand restrided into scratch (K % 8, N % 8) */
   int lda, ldb;          /* leading dimensions the tensor maps use */
-  int tma_store;         /* 1: TMA-store epilogue (N % 8 == 0), 0: SIMT stores */
+  int tma_store;         /* 1: TMA-store epilogue; 0: SIMT stores (N % 8 != 0, beta == 0) */
   size_t scratch_bytes;  /* scratch needed for restrided operands */
   int sched_static;      /* 1: cluster c takes tiles c, c + clusters, ... (short tiles, or all
                             tiles co-resident); 0: cluster launch control */
   int ksplit;            /* > 1: split-K, a cluster of ksplit one-CTA tiles shares each tile's
                             k-blocks (grid_ctas = tiles * ksplit) */
   int epi_warps;         /* epilogue warps per CTA: 4, or 8 where the epilogue sets the pace */
+  int pad_c;             /* C computed in a 16-byte-strided copy (N % 8 != 0, beta != 0),
+                            then compacted */
+  int ldc;               /* row stride of the C the kernel writes */
 } hgemm_plan_t;
 
 /* `aligned16` says whether A, B and C all start on 16-byte boundaries; `sm_count` and

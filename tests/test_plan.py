@@ -15,21 +15,25 @@ def test_noop_and_fallback_paths():
     assert hg.plan(128, 128, 64, aligned16=False, **B200)["path"] == 2
 
 
-@pytest.mark.parametrize("M,N,K,pad_a,pad_b,tma", [
-    (4095, 4095, 4095, 1, 1, 0),     # both operands restrided, SIMT stores (N odd)
-    (4096, 4095, 4096, 0, 1, 0),
-    (2048, 2047, 2048, 0, 1, 0),
-    (3000, 1000, 2000, 0, 0, 1),     # aligned strides, ragged tiles only
-    (1023, 1, 1025, 1, 1, 0),
-    (8192, 8192, 8192, 0, 0, 1),
+@pytest.mark.parametrize("M,N,K,beta,pad_a,pad_b,pad_c,tma", [
+    (4095, 4095, 4095, 0.0, 1, 1, 0, 0),   # both operands restrided, SIMT stores (N odd)
+    (4095, 4095, 4095, 0.5, 1, 1, 1, 1),   # beta != 0: C computed in a padded copy
+    (4096, 4095, 4096, 0.0, 0, 1, 0, 0),
+    (4096, 4095, 4096, 0.5, 0, 1, 1, 1),
+    (2048, 2047, 2048, 0.5, 0, 1, 1, 1),
+    (3000, 1000, 2000, 0.5, 0, 0, 0, 1),   # aligned strides, ragged tiles only
+    (1023, 1, 1025, 0.0, 1, 1, 0, 0),
+    (8192, 8192, 8192, 0.0, 0, 0, 0, 1),
 ])
-def test_restride_and_epilogue_choice(M, N, K, pad_a, pad_b, tma):
-    p = hg.plan(M, N, K, **B200)
+def test_restride_and_padded_c(M, N, K, beta, pad_a, pad_b, pad_c, tma):
+    p = hg.plan(M, N, K, beta=beta, **B200)
     assert p["path"] == 1
-    assert (p["pad_a"], p["pad_b"], p["tma_store"]) == (pad_a, pad_b, tma)
+    assert (p["pad_a"], p["pad_b"], p["pad_c"], p["tma_store"]) == (pad_a, pad_b, pad_c, tma)
     assert p["lda"] % 8 == 0 and p["ldb"] % 8 == 0
-    assert p["lda"] >= K and p["ldb"] >= N
-    want = 2 * ((M * p["lda"] if pad_a else 0) + (K * p["ldb"] if pad_b else 0))
+    assert p["lda"] >= K and p["ldb"] >= N and p["ldc"] >= N
+    assert p["ldc"] == (p["ldb"] if pad_c else N)
+    want = 2 * ((M * p["lda"] if pad_a else 0) + (K * p["ldb"] if pad_b else 0) +
+                (M * p["ldc"] if pad_c else 0))
     assert p["scratch_bytes"] == want
 
 
