@@ -133,19 +133,16 @@ struct KParams {
 };
 
 // Other destinations of every C tile (e.g. the C buffers of peer GPUs mapped into this
-// process): the epilogue issues the same TMA store once more per map, so a row-sharded GEMM
-// delivers its rows to every rank while it computes them.
+// process): M x N row-major buffers with row stride N. The epilogue warps copy each staged
+// 32 x 64 chunk to them with coalesced 16-byte stores after the local TMA store, so a
+// row-sharded GEMM delivers its rows to every rank while it computes them (the SM's TMA
+// unit only carries the local C and the operand loads; a TMA-store variant of the copy
+// measured the same on 4 B200s).
 constexpr int kMaxPeers = 7;
 struct PeerMaps {
-  CUtensorMap m[kMaxPeers];  // TMA stores (lsu == 0)
-  __half *ptr[kMaxPeers];    // same M x N row-major buffers for 16-byte stores (lsu == 1)
+  __half *ptr[kMaxPeers];
   int n;
-  int lsu;  // 1: the epilogue warps copy each staged chunk to the peers with 16-byte stores,
-            // so the SM's TMA unit only carries the local C and the operand loads
 };
-#ifndef HGEMM_PEER_PUSH_LSU
-#define HGEMM_PEER_PUSH_LSU 1
-#endif
 // C stores carry an L2 evict-first policy from this K on: with long main loops the A and B
 // tiles are re-read from L2 many times and the streamed C should not displace them
 // (8192^3: +1.4%); with short K the whole C fits in L2 and is written back after the
@@ -319,7 +316,6 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
     ptx::prefetch_tmap(&tmB);
     if (TMA_EPI) {
       ptx::prefetch_tmap(&tmC);
-      for (int d = 0; d < npeer; ++d) ptx::prefetch_tmap(&peers.m[d]);
     }
   }
   if (warp == 1) {
@@ -993,13 +989,10 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
               if (lane == 0) {
                 if (row0 < p.M && ccol < p.N) {
                   store_c(&tmC, ptx::smem_u32(stg0) + buf, ccol, row0);
-                  if (!peers.lsu)
-                    for (int d = 0; d < npeer; ++d)
-                      store_c(&peers.m[d], ptx::smem_u32(stg0) + buf, ccol, row0);
                 }
                 ptx::bulk_commit_group();
               }
-              if (npeer > 0 && peers.lsu) push_peers(stg0 + buf, row0, ccol);
+              if (npeer > 0) push_peers(stg0 + buf, row0, ccol);
             }
           }
           if (aborted) break;
@@ -1131,13 +1124,10 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
           if (lane == 0) {
             if (row0 < p.M && ccol < p.N) {
               store_c(&tmC, ptx::smem_u32(stg), ccol, row0);
-              if (!peers.lsu)
-                for (int d = 0; d < npeer; ++d)
-                  store_c(&peers.m[d], ptx::smem_u32(stg), ccol, row0);
             }
             ptx::bulk_commit_group();  // one group per chunk, empty when nothing was stored
           }
-          if (npeer > 0 && peers.lsu) push_peers(stg, row0, ccol);
+          if (npeer > 0) push_peers(stg, row0, ccol);
         } else {
           // C's rows are not 16-byte aligned: stage through smem, then coalesced 2-byte
           // accesses (lanes along a row), predicated on the M/N edges.
@@ -1780,12 +1770,9 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
     for (int i = 0; i < npeers; ++i) {
       if (!peer_C[i] || reinterpret_cast<uintptr_t>(peer_C[i]) % 16 != 0)
         return HGEMM_ERR_NOT_FUSABLE;
-      if (!encode_2d(&peers.m[i], peer_C[i], M, N, N, EPI_ROWS, EPI_COLS))
-        return HGEMM_ERR_TENSOR_MAP;
       peers.ptr[i] = peer_C[i];
     }
     peers.n = npeers;
-    peers.lsu = HGEMM_PEER_PUSH_LSU;
   }
   const int flav = !tma_epi ? kFlavSimt
                    : pl.ksplit > 1 ? kFlavSplit
