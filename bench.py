@@ -572,8 +572,10 @@ def main():
             "check_rel_l2_vs_cublas": spot_l2,
             "device_status": st_dev,
             "e2e": e2e,
-            "gpu_launches": args.steps * (1 if (comm is None or args.exchange == "peer")
-                                          else max(1, args.chunks)),
+            # our kernels per step: the GEMM; with the peer exchange also the one-warp
+            # barrier kernel; with NCCL one GEMM per chunk (NCCL's own kernels not counted)
+            "gpu_launches": args.steps * (1 if comm is None else
+                                          2 if args.exchange == "peer" else max(1, args.chunks)),
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
