@@ -1632,6 +1632,13 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
         tile = c.tile;
       }
     }
+    // A single wave of pair tiles with K >= 1024 runs cold and TMA-latency bound; when the
+    // 128x64 one-CTA tiles also fit in one wave they keep twice the SMs and more stages
+    // busy (B200: 1024^3 0.62 -> 0.66 of cuBLAS, 384x2048x2048 0.55 -> 0.60).
+    const double pair_tiles = static_cast<double>(ceil_div(M, 2 * CTA_M)) * ceil_div(N, kTiles[tile].bn);
+    const double t64 = static_cast<double>(ceil_div(M, CTA_M)) * ceil_div(N, 64);
+    if (kTiles[tile].pair == 2 && pair_tiles <= pair_slots && kb >= 16 && t64 <= sm_count)
+      tile = kT128x64;
   }
   const TileInfo &ti = kTiles[tile];
   pl->pair = ti.pair;
