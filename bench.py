@@ -9,9 +9,10 @@ One step = one GEMM (plus, with N GPUs, the all-gather of C). At N=1 the shape i
 configuration the metric is quoted on. With N GPUs (torchrun, one process per GPU) the
 default job keeps the per-GPU work fixed (weak scaling): M = 8192*N rows split by rank, B
 replicated, and every rank ends each step with the whole C: one kernel per rank computes its
-rows and its epilogue TMA-stores each finished tile into every rank's C over NVLink (peer
-buffers mapped with CUDA IPC), followed by a 4-byte NCCL barrier (`--exchange nccl`: the GEMM
-then an NCCL all-gather instead). `--workload sharded32k`
+rows and its epilogue stores each finished tile into every rank's C over NVLink (16-byte
+stores into peer buffers mapped with CUDA IPC), followed by a one-warp device flag barrier
+across the ranks (`--exchange nccl`, or when some rank cannot map the peers' buffers: the
+GEMM then an NCCL all-gather instead). `--workload sharded32k`
 runs BASELINE configs[4] instead: the 32768x32768x16384 GEMM split by rows over the N GPUs
 (strong scaling).
 
@@ -384,6 +385,7 @@ def main():
     flush = torch.empty(3 * l2, dtype=torch.uint8, device=dev)
 
     comm = None
+    peer_fallback = None
     if world > 1:
         import ctypes
         idbuf = torch.zeros(128, dtype=torch.uint8, device=dev)
@@ -405,7 +407,9 @@ def main():
             st = hg.lib.hgemm_comm_register_output(comm, C.data_ptr(),
                                                    C.numel() * C.element_size())
             if st != 0:
-                raise SystemExit(f"peer exchange unavailable: {hg.status_string(st)}")
+                # collective agreement: every rank sees the same status and falls back together
+                peer_fallback = hg.status_string(st)
+                args.exchange = "nccl"
 
     def ours():
         if comm is None:
@@ -553,10 +557,12 @@ def main():
                                     f"gemm_{M}x{N}x{K}_rowsharded_" +
                                     ("peerstore" if args.exchange == "peer" else "allgather")),
                        "exchange": None if world == 1 else (
-                           "fused GEMM epilogue TMA-stores every tile to all ranks' C over "
-                           "NVLink (CUDA IPC peer mappings) + 4-byte NCCL barrier"
+                           "fused GEMM epilogue stores every tile to all ranks' C over "
+                           "NVLink (16-byte stores, CUDA IPC peer mappings) + device flag barrier"
                            if args.exchange == "peer" else
-                           f"NCCL all-gather / send-recv, {args.chunks} chunk(s)"),
+                           f"NCCL all-gather / send-recv, {args.chunks} chunk(s)" +
+                           (f" (peer mapping unavailable: {peer_fallback})"
+                            if peer_fallback else "")),
                        "M": M, "N": N, "K": K, "alpha": 1.0, "beta": 0.0,
                        "rows_per_gpu": Ml, "parallelism": f"rowshard{world}",
                        "l2": "flushed (3x L2 memset) before every timed launch",
