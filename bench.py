@@ -66,6 +66,9 @@ def parse():
                     help="the reference's 31-shape grid (perf_shapes.h) plus the ragged and thin-K "
                          "configs, one JSON line per shape, ours vs cuBLAS interleaved")
     ap.add_argument("--grid-reps", type=int, default=25)
+    ap.add_argument("--grid-shapes", default="",
+                    help="with --grid: only these shapes, comma-separated MxNxK[:alpha/beta] "
+                         "(e.g. 1024x1024x1024,3000x1000x2000:1.5/0.5)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -282,6 +285,13 @@ def run_grid(args):
                         dtype=torch.uint8, device=dev)
     cases = [(M, N, K, 1.0, 0.0) for (M, N, K) in GRID_SHAPES]
     cases += [(M, N, K, 1.5, 0.5) for (M, N, K) in GRID_RAGGED]
+    if args.grid_shapes:
+        cases = []
+        for spec in args.grid_shapes.split(","):
+            dims, _, ab = spec.partition(":")
+            M, N, K = (int(v) for v in dims.split("x"))
+            al, be = (float(v) for v in ab.split("/")) if ab else (1.0, 0.0)
+            cases.append((M, N, K, al, be))
     for i, (M, N, K, al, be) in enumerate(cases):
         A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device=dev), 0x9E3779B9 ^ i)
         B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device=dev), 0x85EBCA6B ^ i)

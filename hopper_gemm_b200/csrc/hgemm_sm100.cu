@@ -841,58 +841,68 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
 #pragma unroll 1
         for (int ci = Cfg::EPI_WARPS * split + ew; okr && ci < 4 * (BN / 64); ci += workers) {
           const int rb = ci & 3, cb = ci >> 2;
-          float f[64];
-#pragma unroll 1
-          for (int t = 0; t < ksplit; ++t) {
-            const uint32_t tb = (t == split) ? part : ptx::mapa(part, static_cast<uint32_t>(t));
-#pragma unroll 8
-            for (int i = 0; i < 16; ++i) {
-              const int rr = 32 * rb + 2 * i + lhalf;
-              const uint32_t g = static_cast<uint32_t>(16 * cb + lg);
-              const uint32_t a = tb + static_cast<uint32_t>(rr) * (BN * 4) +
-                                 ((g ^ static_cast<uint32_t>(rr & 7)) << 4);
-              const float4 x = (t == split) ? ptx::ld_shared_v4f(a) : ptx::ld_shared_cluster_v4f(a);
-              if (t == 0) {
-                f[4 * i] = x.x; f[4 * i + 1] = x.y; f[4 * i + 2] = x.z; f[4 * i + 3] = x.w;
-              } else {
-                f[4 * i] += x.x; f[4 * i + 1] += x.y; f[4 * i + 2] += x.z; f[4 * i + 3] += x.w;
-              }
-            }
-          }
           const int gcol = col0 + 64 * cb + 4 * lg;  // this lane's first column
-#pragma unroll
-          for (int e = 0; e < 64; ++e) f[e] *= alpha;
-          if (beta != 0.0f) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int grow = tm * CTA_M + 32 * rb + 2 * i + lhalf;
-              // ldc % 8 == 0: a group of 4 halves that starts inside a row ends inside its
-              // stride (pad columns of a restrided C hold zeros and are never stored)
-              if (grow < p.M && gcol < p.N) {
-                const uint2 u = __ldg(reinterpret_cast<const uint2 *>(
-                    p.C + static_cast<long long>(grow) * p.ldc + gcol));
-                const float2 c0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
-                const float2 c1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
-                f[4 * i] = fmaf(beta, c0.x, f[4 * i]);
-                f[4 * i + 1] = fmaf(beta, c0.y, f[4 * i + 1]);
-                f[4 * i + 2] = fmaf(beta, c1.x, f[4 * i + 2]);
-                f[4 * i + 3] = fmaf(beta, c1.y, f[4 * i + 3]);
-              }
-            }
-          }
           uint8_t *stg = stg0 + (chunk_ctr % EB) * (EPI_ROWS * 128);
           ++chunk_ctr;
           if (lane == 0) ptx::bulk_wait_group_read<EB - 1>();
           __syncwarp();
-          // staging layout of the TMA store: row r's 16-byte group j at r*128 + (j ^ (r&7))*16;
-          // this lane's 4 halves are the (lg&1) half of group lg/2.
+          // Two halves of 16 rows each, fully unrolled so the 32 sums stay in registers (a
+          // 64-float array indexed from a partly unrolled loop lives in local memory and
+          // made one chunk's reduction ~20 K cycles).
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float f[32];
+#pragma unroll 1
+            for (int t = 0; t < ksplit; ++t) {
+              const uint32_t tb = (t == split) ? part : ptx::mapa(part, static_cast<uint32_t>(t));
+              float4 x[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int r = 2 * i + lhalf;
-            uint2 w;
-            w.x = pack_half2(f[4 * i], f[4 * i + 1]);
-            w.y = pack_half2(f[4 * i + 2], f[4 * i + 3]);
-            *reinterpret_cast<uint2 *>(stg + sw128_off(r, lg >> 1) + 8 * (lg & 1)) = w;
+              for (int i = 0; i < 8; ++i) {
+                const int rr = 32 * rb + 2 * (8 * h + i) + lhalf;
+                const uint32_t g = static_cast<uint32_t>(16 * cb + lg);
+                const uint32_t a = tb + static_cast<uint32_t>(rr) * (BN * 4) +
+                                   ((g ^ static_cast<uint32_t>(rr & 7)) << 4);
+                x[i] = (t == split) ? ptx::ld_shared_v4f(a) : ptx::ld_shared_cluster_v4f(a);
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                if (t == 0) {
+                  f[4 * i] = x[i].x; f[4 * i + 1] = x[i].y; f[4 * i + 2] = x[i].z; f[4 * i + 3] = x[i].w;
+                } else {
+                  f[4 * i] += x[i].x; f[4 * i + 1] += x[i].y; f[4 * i + 2] += x[i].z; f[4 * i + 3] += x[i].w;
+                }
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 32; ++e) f[e] *= alpha;
+            if (beta != 0.0f) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int grow = tm * CTA_M + 32 * rb + 2 * (8 * h + i) + lhalf;
+                // ldc % 8 == 0: a group of 4 halves that starts inside a row ends inside its
+                // stride (pad columns of a restrided C hold zeros and are never stored)
+                if (grow < p.M && gcol < p.N) {
+                  const uint2 u = __ldg(reinterpret_cast<const uint2 *>(
+                      p.C + static_cast<long long>(grow) * p.ldc + gcol));
+                  const float2 c0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+                  const float2 c1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+                  f[4 * i] = fmaf(beta, c0.x, f[4 * i]);
+                  f[4 * i + 1] = fmaf(beta, c0.y, f[4 * i + 1]);
+                  f[4 * i + 2] = fmaf(beta, c1.x, f[4 * i + 2]);
+                  f[4 * i + 3] = fmaf(beta, c1.y, f[4 * i + 3]);
+                }
+              }
+            }
+            // staging layout of the TMA store: row r's 16-byte group j at r*128 + (j ^ (r&7))*16;
+            // this lane's 4 halves are the (lg&1) half of group lg/2.
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 2 * (8 * h + i) + lhalf;
+              uint2 w;
+              w.x = pack_half2(f[4 * i], f[4 * i + 1]);
+              w.y = pack_half2(f[4 * i + 2], f[4 * i + 3]);
+              *reinterpret_cast<uint2 *>(stg + sw128_off(r, lg >> 1) + 8 * (lg & 1)) = w;
+            }
           }
           ptx::fence_proxy_async_smem();
           __syncwarp();
