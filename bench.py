@@ -270,17 +270,19 @@ GRID_RAGGED = [(4095, 4095, 4095), (4096, 4095, 4096), (2048, 2047, 2048), (3000
 
 def run_grid(args):
     """Reference methodology per shape (three_way.cu): hash-filled A/B, 5 interleaved
-    warm-ups, then `reps` rounds of {3x L2 memset, event, one launch, event} for ours and for
-    cuBLAS; median TFLOPS and the median of per-round paired ratios. The ragged configs are
-    also run with alpha=1.5, beta=0.5 (BASELINE configs[1])."""
+    warm-ups, then `reps` rounds of {3x L2 memset, event, one launch, event} for ours, for
+    cuBLAS and (16-byte aligned shapes, when it was built) for the CUTLASS SM100 comparator;
+    median TFLOPS and the median of per-round paired ratios. The ragged configs are also run
+    with alpha=1.5, beta=0.5 (BASELINE configs[1])."""
     import torch
     import hopper_gemm_b200 as hg
-    from hopper_gemm_b200._native import cublas_ref_lib
+    from hopper_gemm_b200._native import cublas_ref_lib, cutlass_ref_lib
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
     cub = cublas_ref_lib()
+    cut = cutlass_ref_lib()  # third column (None if the comparator was not built)
     flush = torch.empty(3 * torch.cuda.get_device_properties(dev).L2_cache_size,
                         dtype=torch.uint8, device=dev)
     cases = [(M, N, K, 1.0, 0.0) for (M, N, K) in GRID_SHAPES]
@@ -298,6 +300,8 @@ def run_grid(args):
         C = hash_fill_(torch.empty((M, N), dtype=torch.float16, device=dev), 0x1234 ^ i)
         R = C.clone()
         C0 = C.clone()
+        T = C.clone()
+        use_cut = cut is not None and N % 8 == 0 and K % 8 == 0
 
         def ours():
             st = hg.lib.hgemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, al, be, sptr)
@@ -306,6 +310,12 @@ def run_grid(args):
 
         def cbl():
             cub.hgemm_cublas_ref(A.data_ptr(), B.data_ptr(), R.data_ptr(), M, N, K, al, be, sptr)
+
+        def ctl():
+            st = cut.hgemm_cutlass_ref(A.data_ptr(), B.data_ptr(), T.data_ptr(), M, N, K, al, be,
+                                       sptr)
+            if st != 0:
+                raise RuntimeError(f"hgemm_cutlass_ref status {st}")
 
         def sample(fn):
             e0 = torch.cuda.Event(enable_timing=True)
@@ -320,18 +330,27 @@ def run_grid(args):
         # correctness of this shape against cuBLAS from the same C input
         C.copy_(C0)
         R.copy_(C0)
+        T.copy_(C0)
         ours()
         cbl()
+        if use_cut:
+            ctl()
         torch.cuda.synchronize()
         l2 = float((C.float() - R.float()).norm() / (R.float().norm() + 1e-30))
+        l2t = (float((C.float() - T.float()).norm() / (T.float().norm() + 1e-30))
+               if use_cut else None)
         for _ in range(5):
             ours()
             cbl()
+            if use_cut:
+                ctl()
         torch.cuda.synchronize()
-        to, tc = [], []
+        to, tc, tt = [], [], []
         for _ in range(args.grid_reps):
             to.append(sample(ours))
             tc.append(sample(cbl))
+            if use_cut:
+                tt.append(sample(ctl))
         fl = 2.0 * M * N * K
         plan = hg.plan(M, N, K, beta=be)
         print(json.dumps({
@@ -339,9 +358,13 @@ def run_grid(args):
             "ours_tflops": fl / (statistics.median(to) * 1e-3) / 1e12,
             "cublas_tflops": fl / (statistics.median(tc) * 1e-3) / 1e12,
             "paired_ratio_median": statistics.median(c / o for o, c in zip(to, tc)),
-            "rel_l2_vs_cublas": l2, "tile": f"{plan['tile_m']}x{plan['tile_n']}",
+            "cutlass_tflops": fl / (statistics.median(tt) * 1e-3) / 1e12 if tt else None,
+            "paired_ratio_vs_cutlass": (statistics.median(t / o for o, t in zip(to, tt))
+                                        if tt else None),
+            "rel_l2_vs_cublas": l2, "rel_l2_vs_cutlass": l2t,
+            "tile": f"{plan['tile_m']}x{plan['tile_n']}",
             "restride": bool(plan["pad_a"] or plan["pad_b"])}), flush=True)
-        del A, B, C, R, C0
+        del A, B, C, R, C0, T
         torch.cuda.empty_cache()
 
 

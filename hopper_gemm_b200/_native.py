@@ -9,6 +9,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libhgemm_b200.so")
 CUBLAS_REF_PATH = os.path.join(HERE, "libhgemm_cublas_ref.so")
+CUTLASS_REF_PATH = os.path.join(HERE, "libhgemm_cutlass_ref.so")
 
 HGEMM_OK = 0
 HGEMM_ERR_INVALID_ARG = 1
@@ -105,3 +106,20 @@ def cublas_ref_lib():
         L.hgemm_cublas_ref.argtypes = _GEMM + [_vp]
         _cublas = L
     return _cublas
+
+
+_cutlass = None
+
+
+def cutlass_ref_lib():
+    """The CUTLASS SM100 comparator (bench/test infrastructure, not the product), or None
+    when it was not built (no CUTLASS headers on the build machine)."""
+    global _cutlass
+    if _cutlass is None:
+        if not os.path.exists(CUTLASS_REF_PATH):
+            return None
+        L = ctypes.CDLL(CUTLASS_REF_PATH, mode=ctypes.RTLD_LOCAL)
+        L.hgemm_cutlass_ref.restype = _i
+        L.hgemm_cutlass_ref.argtypes = _GEMM + [_vp]
+        _cutlass = L
+    return _cutlass

@@ -3,6 +3,9 @@
 Produces, next to this file:
   libhgemm_b200.so       the GEMM product: tcgen05 kernel, dispatcher, C ABI, NCCL row shards
   libhgemm_cublas_ref.so the cuBLAS comparator used by bench.py and the GPU tests
+  libhgemm_cutlass_ref.so the CUTLASS SM100 comparator (third grid column, cross-check tests),
+                         built when CUTLASS's headers are found (the copies vendored in the
+                         flashinfer or tilelang wheels); skipped with a notice otherwise
 Both are compiled with `-gencode arch=compute_100a,code=sm_100a`; nvcc cross-compiles them on
 a machine without a GPU.
 """
@@ -18,6 +21,26 @@ INCLUDE = os.path.join(ROOT, "include")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB = os.path.join(HERE, "libhgemm_b200.so")
 CUBLAS_LIB = os.path.join(HERE, "libhgemm_cublas_ref.so")
+CUTLASS_LIB = os.path.join(HERE, "libhgemm_cutlass_ref.so")
+
+
+def _cutlass_include():
+    """CUTLASS include dirs (include/ and tools/util/include/) from an installed wheel that
+    vendors them, located without importing the package; None if there is none."""
+    import importlib.util
+    for pkg, sub in (("flashinfer", ("data", "cutlass")), ("tilelang", ("3rdparty", "cutlass"))):
+        try:
+            spec = importlib.util.find_spec(pkg)
+        except (ImportError, ValueError):
+            spec = None
+        if not spec or not spec.submodule_search_locations:
+            continue
+        root = os.path.join(list(spec.submodule_search_locations)[0], *sub)
+        inc, util = os.path.join(root, "include"), os.path.join(root, "tools", "util", "include")
+        if os.path.exists(os.path.join(inc, "cutlass", "gemm", "collective",
+                                       "collective_builder.hpp")) and os.path.isdir(util):
+            return [inc, util]
+    return None
 
 
 def _nvcc():
@@ -51,6 +74,15 @@ def build(force=False, verbose=True, extra_flags=()):
     csrc = [os.path.join(CSRC, "cublas_ref.cu")]
     if force or _stale(CUBLAS_LIB, csrc):
         _run([nvcc] + common + ["-shared", "-o", CUBLAS_LIB] + csrc + ["-lcublas"], verbose)
+    tsrc = [os.path.join(CSRC, "cutlass_ref.cu")]
+    if force or _stale(CUTLASS_LIB, tsrc):
+        inc = _cutlass_include()
+        if inc is None:
+            print("note: CUTLASS headers not found; libhgemm_cutlass_ref.so (comparator) skipped",
+                  flush=True)
+        else:
+            _run([nvcc] + common + ["--expt-relaxed-constexpr"] + ["-I" + d for d in inc] +
+                 ["-shared", "-o", CUTLASS_LIB] + tsrc, verbose)
     return LIB
 
 
