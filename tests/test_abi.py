@@ -64,3 +64,19 @@ def test_shard_rows_partition(M, nr):
         covered.extend(range(b, b + c))
         assert c in (M // nr, M // nr + 1)
     assert covered == list(range(M))
+
+
+def test_comparators_load_and_export_their_entry_points():
+    """bench.py and the GPU tests' comparators: cuBLAS always, CUTLASS SM100 when it was built
+    (the build skips it only where no CUTLASS headers are installed)."""
+    import hopper_gemm_b200._native as nat
+    assert hasattr(ctypes.CDLL(nat.CUBLAS_REF_PATH), "hgemm_cublas_ref")
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "_hgemm_build", os.path.join(ROOT, "hopper_gemm_b200", "build.py"))
+    hb = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(hb)
+    if hb._cutlass_include() is None:
+        pytest.skip("no CUTLASS headers on this machine")
+    lib = nat.cutlass_ref_lib()
+    assert lib is not None and hasattr(lib, "hgemm_cutlass_ref")
