@@ -6,8 +6,8 @@
 // place as C = alpha * A @ B + beta * C, fp16 operands and output, fp32 accumulation.
 //
 // Kernel choice: 1-SM UMMA (tcgen05.mma cta_group::1), 128 x 256 x 64 tiles, cluster 1 x 1 x 1,
-// so its operand loads are plain TMA tile loads (this repository runs multi-GPU jobs and
-// therefore contains no cluster-multicast loads anywhere). The library owns one grow-only
+// so its operand loads are plain per-CTA TMA tile loads, like every load in this repository
+// (whose multi-GPU jobs must not carry loads shared across a cluster). The library owns one grow-only
 // workspace per device for CUTLASS's tile scheduler.
 #include <cuda_runtime.h>
 
