@@ -22,6 +22,13 @@ cuBLAS cublasGemmEx timed interleaved on the same data; W >= 3 warm-up steps; K 
 steps bracketed by barrier + synchronize; the max over ranks. `value` = whole-job TFLOPS over
 the K steps; `e2e` = the same metric through the C ABI (`solve` at N=1) with host buffers
 (pinned H2D of A and B, D2H of C inside the timed region).
+
+After the timed steps every rank checks its whole C (its own rows and the rows the other
+ranks stored into it) against the same GEMM run on one GPU in one launch (bit equality) and
+against cuBLAS (rel_l2); the line reports the worst rank. Every run also measures BASELINE
+configs[4] at the same N (`config5`: the 32768x32768x16384 GEMM split by rows over the GPUs,
+strong scaling, same exchange and the same whole-C checks), unless --no-config5.
+`--grid` runs each shape of the grid in a process of its own.
 """
 import argparse
 import json
@@ -38,6 +45,11 @@ sys.path.insert(0, ROOT)
 FALLBACK_PEAK_TFLOPS = 1590.0
 DEFAULT_CHUNKS = 1  # --exchange nccl: measured fastest on 2 B200s (one in-place all-gather)
 FALLBACK_HBM_GBS = 6650.0
+# Peer copy over NVLink 5, measured on this pool's B200s (per direction per GPU); the bound
+# for the bytes a fused step must move to the other ranks.
+NVLINK_PEER_GBS = 770.0
+# the row-sharded 32768 x 32768 x 16384 GEMM.
+C5_M, C5_N, C5_K = 32768, 32768, 16384
 
 
 def parse():
@@ -69,6 +81,12 @@ def parse():
     ap.add_argument("--grid-shapes", default="",
                     help="with --grid: only these shapes, comma-separated MxNxK[:alpha/beta] "
                          "(e.g. 1024x1024x1024,3000x1000x2000:1.5/0.5)")
+    ap.add_argument("--no-config5", dest="config5", action="store_false",
+                    help="skip the BASELINE configs[4] block (32768x32768x16384 split by rows "
+                         "over the N GPUs, strong scaling) that every run adds by default")
+    ap.add_argument("--config5-steps", type=int, default=10)
+    ap.add_argument("--grid-child", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--grid-index", type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -294,7 +312,16 @@ def run_grid(args):
             M, N, K = (int(v) for v in dims.split("x"))
             al, be = (float(v) for v in ab.split("/")) if ab else (1.0, 0.0)
             cases.append((M, N, K, al, be))
-    for i, (M, N, K, al, be) in enumerate(cases):
+    if not args.grid_child:
+        # One shape per process, as the reference's harness runs them (Makefile:78-79,
+        # three_way.cu's single-shape mode): a shape measured after others inherits their heat.
+        for i, (M, N, K, al, be) in enumerate(cases):
+            spec = f"{M}x{N}x{K}:{al}/{be}"
+            subprocess.run([sys.executable, os.path.abspath(__file__), "--grid", "--grid-child",
+                            "--grid-shapes", spec, "--grid-index", str(i),
+                            "--grid-reps", str(args.grid_reps)], check=True)
+        return
+    for i, (M, N, K, al, be) in enumerate(cases, start=args.grid_index):
         A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device=dev), 0x9E3779B9 ^ i)
         B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device=dev), 0x85EBCA6B ^ i)
         C = hash_fill_(torch.empty((M, N), dtype=torch.float16, device=dev), 0x1234 ^ i)
@@ -368,6 +395,84 @@ def run_grid(args):
         torch.cuda.empty_cache()
 
 
+def fused_roofline(rows, N, K, world, step_ms, peak_tflops):
+    """Roofline of one rank's fused step (GEMM whose epilogue stores every tile into the other
+    ranks' C over NVLink): the target time is the slower of the math at the measured GEMM peak
+    and the rows this rank must send at the measured peer-copy bandwidth; frac = target / the
+    measured step (kernel + exit barrier)."""
+    flops = 2.0 * rows * N * K
+    link_bytes = (world - 1) * rows * N * 2.0  # sent per rank (and received, by symmetry)
+    t_math = flops / (peak_tflops * 1e12)
+    t_link = link_bytes / (NVLINK_PEER_GBS * 1e9)
+    step_s = step_ms * 1e-3
+    if t_math >= t_link:
+        return {"bound": "tensor", "achieved": flops / step_s / 1e12, "peak": peak_tflops,
+                "unit": "TFLOP/s", "frac": t_math / step_s, "traffic": None,
+                "nvlink_gbs_per_direction": link_bytes / step_s / 1e9,
+                "kernel": "hgemm_tc_kernel peer-store flavour (+ one-warp exit barrier)"}
+    return {"bound": "nvlink", "achieved": link_bytes / step_s / 1e9, "peak": NVLINK_PEER_GBS,
+            "unit": "GB/s", "frac": t_link / step_s, "traffic": None,
+            "tflops": flops / step_s / 1e12,
+            "kernel": "hgemm_tc_kernel peer-store flavour (+ one-warp exit barrier)"}
+
+
+class Job:
+    """One row-sharded GEMM job on this rank: A rows [rb, rb + Ml) of an M x K matrix, B
+    replicated, C the full M x N on every rank (gathered by hgemm_sharded_rank for N > 1)."""
+
+    def __init__(self, hg, dev, rank, world, M, N, K, a_blocks):
+        import torch
+        self.hg, self.dev, self.rank, self.world = hg, dev, rank, world
+        self.M, self.N, self.K = M, N, K
+        self.rb, self.Ml = hg.shard_rows(M, world, rank)
+        self.a_blocks = a_blocks  # (row_begin, rows, seed) blocks that make up the full A
+        self.A = self.fill_a(self.rb, self.Ml)
+        self.B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device=dev), 0x85EBCA6B)
+        self.C = torch.empty((M, N), dtype=torch.float16, device=dev)
+
+    def fill_a(self, r0, rows):
+        """Rows [r0, r0 + rows) of the full A, each block filled with its own seed."""
+        import torch
+        out = torch.empty((rows, self.K), dtype=torch.float16, device=self.dev)
+        for b0, n, seed in self.a_blocks:
+            lo, hi = max(b0, r0), min(b0 + n, r0 + rows)
+            if lo < hi:
+                blk = hash_fill_(torch.empty((n, self.K), dtype=torch.float16, device=self.dev),
+                                 seed)
+                out[lo - r0:hi - r0].copy_(blk[lo - b0:hi - b0])
+                del blk
+        return out
+
+    def full_check(self):
+        """The whole gathered C on this rank against (a) the same GEMM computed here on one GPU
+        in one launch (bit equality: every row block is the same kernel's arithmetic) and (b)
+        cuBLAS on the full problem (rel_l2). Untimed."""
+        import torch
+        from hopper_gemm_b200._native import cublas_ref_lib
+        torch.cuda.synchronize()
+        A = self.fill_a(0, self.M)
+        ref = torch.empty_like(self.C)
+        st = self.hg.lib.hgemm_launch(A.data_ptr(), self.B.data_ptr(), ref.data_ptr(), self.M,
+                                      self.N, self.K, 1.0, 0.0, None)
+        assert st == 0, self.hg.status_string(st)
+        torch.cuda.synchronize()
+        same = bool(torch.equal(self.C.view(torch.int16), ref.view(torch.int16)))
+        st = cublas_ref_lib().hgemm_cublas_ref(A.data_ptr(), self.B.data_ptr(), ref.data_ptr(),
+                                               self.M, self.N, self.K, 1.0, 0.0, None)
+        assert st == 0
+        torch.cuda.synchronize()
+        num = den = 0.0
+        step = max(1, (1 << 27) // max(self.N, 1))
+        for r0 in range(0, self.M, step):
+            c = self.C[r0:r0 + step].float()
+            r = ref[r0:r0 + step].float()
+            num += float(((c - r) ** 2).sum())
+            den += float((r * r).sum())
+        del A, ref
+        torch.cuda.empty_cache()
+        return same, (num / (den + 1e-30)) ** 0.5
+
+
 def main():
     args = parse()
     if args.grid:
@@ -382,7 +487,6 @@ def main():
         run_reference(args, rank, world)
         return
 
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -397,22 +501,22 @@ def main():
 
     if args.workload == "sharded32k":
         # A 32768x16384 split by rows, B 16384x32768 replicated.
-        M, N, K = 32768, 32768, 16384
+        M, N, K = C5_M, C5_N, C5_K
         if M % world:
             raise SystemExit("sharded32k needs a GPU count that divides 32768")
-        Ml = M // world
+        blocks = [(0, M, 0x9E3779B9)]
     else:
-        Ml, N, K = args.M, args.N, args.K
-        M = Ml * world
+        N, K = args.N, args.K
+        M = args.M * world
+        blocks = [(hg.shard_rows(M, world, r)[0], hg.shard_rows(M, world, r)[1], 0x9E3779B9 ^ r)
+                  for r in range(world)]
     if args.chunks <= 0:
         args.chunks = 1 if world == 1 else DEFAULT_CHUNKS
-    flops_job = 2.0 * M * N * K
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
-
-    A = hash_fill_(torch.empty((Ml, K), dtype=torch.float16, device=dev), 0x9E3779B9 ^ rank)
-    B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device=dev), 0x85EBCA6B)
-    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    job = Job(hg, dev, rank, world, M, N, K, blocks)
+    Ml, rb = job.Ml, job.rb
+    flops_job = 2.0 * M * N * K
     R = torch.empty((Ml, N), dtype=torch.float16, device=dev)  # cuBLAS output
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     flush = torch.empty(3 * l2, dtype=torch.uint8, device=dev)
@@ -436,29 +540,40 @@ def main():
         if args.reserved_sms >= 0:
             st = hg.lib.hgemm_comm_set_reserved_sms(comm, args.reserved_sms)
             assert st == 0, hg.status_string(st)
-        if args.exchange == "peer":
-            st = hg.lib.hgemm_comm_register_output(comm, C.data_ptr(),
-                                                   C.numel() * C.element_size())
-            if st != 0:
-                # collective agreement: every rank sees the same status and falls back together
-                peer_fallback = hg.status_string(st)
-                args.exchange = "nccl"
 
-    def ours():
-        if comm is None:
-            st = hg.lib.hgemm_launch_ex(A.data_ptr(), B.data_ptr(), C.data_ptr(), Ml, N, K, 1.0,
-                                        0.0, sptr, args.force_bm, args.force_bn, args.group_m)
-        else:
-            st = hg.lib.hgemm_sharded_rank(comm, A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N,
-                                           K, 1.0, 0.0, args.chunks, sptr)
+    def register(C):
+        """Collective: the fused path for output C (every rank agrees on the outcome)."""
+        nonlocal peer_fallback
+        if comm is None or args.exchange != "peer":
+            return
+        st = hg.lib.hgemm_comm_register_output(comm, C.data_ptr(), C.numel() * C.element_size())
         if st != 0:
-            raise RuntimeError(hg.status_string(st))
+            peer_fallback = hg.status_string(st)
+            args.exchange = "nccl"
 
+    def step_fn(j, A=None, B=None):
+        A = j.A if A is None else A
+        B = j.B if B is None else B
+
+        def fn():
+            if comm is None:
+                st = hg.lib.hgemm_launch_ex(A.data_ptr(), B.data_ptr(), j.C.data_ptr(), j.Ml,
+                                            j.N, j.K, 1.0, 0.0, sptr, args.force_bm,
+                                            args.force_bn, args.group_m)
+            else:
+                st = hg.lib.hgemm_sharded_rank(comm, A.data_ptr(), B.data_ptr(), j.C.data_ptr(),
+                                               j.M, j.N, j.K, 1.0, 0.0, args.chunks, sptr)
+            if st != 0:
+                raise RuntimeError(hg.status_string(st))
+        return fn
+
+    register(job.C)
+    ours = step_fn(job)
     cub = cublas_ref_lib()
 
     def cublas():
-        st = cub.hgemm_cublas_ref(A.data_ptr(), B.data_ptr(), R.data_ptr(), Ml, N, K, 1.0, 0.0,
-                                  sptr)
+        st = cub.hgemm_cublas_ref(job.A.data_ptr(), job.B.data_ptr(), R.data_ptr(), Ml, N, K,
+                                  1.0, 0.0, sptr)
         if st != 0:
             raise RuntimeError("cublas failed")
 
@@ -475,6 +590,12 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t]
 
     # warm-up (interleaved, as three_way.cu:141)
     for _ in range(args.warmup):
@@ -496,44 +617,41 @@ def main():
     t_ours = [a.elapsed_time(b) for a, b in ev_ours]
     t_cub = [a.elapsed_time(b) for a, b in ev_cub]
     region_ms = region0.elapsed_time(region1)
-    tot = torch.tensor([sum(t_ours), sum(t_cub)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
-    ms_ours = float(tot[0]) / args.steps
-    ms_cub = float(tot[1]) / args.steps
+    tot = max_over_ranks([sum(t_ours), sum(t_cub)])
+    ms_ours = tot[0] / args.steps
+    ms_cub = tot[1] / args.steps
     value = flops_job / (ms_ours * 1e-3) / 1e12
-    cub_value = flops_job / world * world / (ms_cub * 1e-3) / 1e12 if world == 1 else None
+    cub_value = flops_job / (ms_cub * 1e-3) / 1e12 if world == 1 else None
     ratios = [c / o for o, c in zip(t_ours, t_cub)]
 
-    # correctness spot check of the benchmarked output against cuBLAS
-    torch.cuda.synchronize()
-    rb = hg.shard_rows(M, world, rank)[0]
-    mine = C[rb:rb + Ml].float()
-    spot_l2 = float((mine - R.float()).norm() / R.float().norm())
+    # the whole gathered C on every rank: bit equality with a one-GPU launch, rel_l2 vs cuBLAS
+    same, full_l2 = job.full_check()
+    chk = max_over_ranks([0.0 if same else 1.0, full_l2])
+    st_dev, where = hg.device_status(clear=False)
+    st_max = max_over_ranks([float(st_dev)])[0]
 
     # end to end through the C ABI with host buffers
     e2e = None
+    e2e_call = None
     if not args.no_e2e:
         hA = torch.empty((Ml, K), dtype=torch.float16, pin_memory=True)
         hB = torch.empty((K, N), dtype=torch.float16, pin_memory=True)
         hC = torch.empty((Ml, N), dtype=torch.float16, pin_memory=True)
-        hA.copy_(A)
-        hB.copy_(B)
-        dA2 = torch.empty_like(A)
-        dB2 = torch.empty_like(B)
+        hA.copy_(job.A)
+        hB.copy_(job.B)
+        dA2 = torch.empty_like(job.A)
+        dB2 = torch.empty_like(job.B)
         e2e_steps = max(3, min(args.steps, 10))
+        e2e_call = step_fn(job, dA2, dB2)
 
         def e2e_step():
             dA2.copy_(hA, non_blocking=True)
             dB2.copy_(hB, non_blocking=True)
             if comm is None:
-                hg.lib.solve(dA2.data_ptr(), dB2.data_ptr(), C.data_ptr(), Ml, N, K, 1.0, 0.0)
+                hg.lib.solve(dA2.data_ptr(), dB2.data_ptr(), job.C.data_ptr(), Ml, N, K, 1.0, 0.0)
             else:
-                st = hg.lib.hgemm_sharded_rank(comm, dA2.data_ptr(), dB2.data_ptr(),
-                                               C.data_ptr(), M, N, K, 1.0, 0.0, args.chunks,
-                                               sptr)
-                assert st == 0
-            hC.copy_(C[rb:rb + Ml], non_blocking=True)
+                e2e_call()
+            hC.copy_(job.C[rb:rb + Ml], non_blocking=True)
 
         for _ in range(2):
             e2e_step()
@@ -545,40 +663,80 @@ def main():
             e2e_step()
         e1.record(stream)
         barrier()
-        t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t[0]) / e2e_steps
+        e2e_ms = max_over_ranks([e0.elapsed_time(e1)])[0] / e2e_steps
         e2e = {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
                "h2d_bytes_per_step": 2 * (Ml * K + K * N), "d2h_bytes_per_step": 2 * Ml * N,
                "ms_per_step": e2e_ms,
                "path": "solve() C ABI, pinned host buffers" if comm is None else
                        "hgemm_sharded_rank() C ABI, pinned host buffers"}
         assert hg.last_status() == 0, hg.status_string(hg.last_status())
+        del hA, hB, hC, dA2, dB2
 
-    # The dominant kernel alone (roofline.achieved): at N=1 that is the timed launch itself;
-    # with N GPUs the step also holds the gather, so the local GEMM is timed separately here.
+    peak, hbm, src = peaks()
     if world == 1:
-        kernel_ms = ms_ours
+        roofline = {"bound": "tensor", "achieved": 2.0 * Ml * N * K / (ms_ours * 1e-3) / 1e12,
+                    "peak": peak, "unit": "TFLOP/s", "traffic": profiled_traffic(Ml, N, K),
+                    "peak_source": f"{src} bf16 dense (burst)"}
+        roofline["frac"] = roofline["achieved"] / peak
     else:
-        def local_gemm():
-            st = hg.lib.hgemm_launch_ex(A.data_ptr(), B.data_ptr(), R.data_ptr(), Ml, N, K, 1.0,
-                                        0.0, sptr, args.force_bm, args.force_bn, args.group_m)
-            if st != 0:
-                raise RuntimeError(hg.status_string(st))
-        local_gemm()
-        kev = [sample(local_gemm) for _ in range(max(3, min(args.steps, 20)))]
-        torch.cuda.synchronize()
-        kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+        # the fused kernel inside the timed step is the dominant kernel
+        roofline = fused_roofline(Ml, N, K, world, ms_ours, peak)
+        roofline["peak_source"] = (f"{src} bf16 dense (burst); NVLink: measured peer copy "
+                                   f"{NVLINK_PEER_GBS:.0f} GB/s per direction")
+    exchange_desc = None if world == 1 else (
+        "fused GEMM epilogue stores every tile to all ranks' C over NVLink (16-byte stores, "
+        "CUDA IPC peer mappings), gated on the peers' step-entry flags, + device flag exit "
+        "barrier" if args.exchange == "peer" else
+        f"NCCL all-gather / send-recv, {args.chunks} chunk(s)" +
+        (f" (peer mapping unavailable: {peer_fallback})" if peer_fallback else ""))
+    main_workload = (f"gemm_{M}x{N}x{K}" if world == 1 else
+                     f"gemm_{M}x{N}x{K}_rowsharded_" +
+                     ("peerstore" if args.exchange == "peer" else "allgather"))
+    gpu_launches = args.steps * (1 if comm is None else
+                                 2 if args.exchange == "peer" else max(1, args.chunks))
+    clk = clocks.summary()
+    del R
 
-    st_dev, where = hg.device_status(clear=False)
+    # BASELINE configs[4] at every N: the 32768 x 32768 x 16384 GEMM split by rows over the
+    # ranks (strong scaling), same exchange, full gathered-C check on every rank.
+    c5 = None
+    if args.config5 and args.workload != "sharded32k" and C5_M % world == 0:
+        j5 = Job(hg, dev, rank, world, C5_M, C5_N, C5_K, [(0, C5_M, 0x9E3779B9)])
+        register(j5.C)  # collective; unmaps the peers' previous output buffers first
+        del job, ours, cublas, e2e_call
+        torch.cuda.empty_cache()
+        f5 = step_fn(j5)
+        for _ in range(3):
+            f5()
+        barrier()
+        with ClockSampler(local_rank) as clk5:
+            ev5 = [sample(f5) for _ in range(args.config5_steps)]
+            barrier()
+        ms5 = max_over_ranks([sum(a.elapsed_time(b) for a, b in ev5)])[0] / len(ev5)
+        same5, l2_5 = j5.full_check()
+        chk5 = max_over_ranks([0.0 if same5 else 1.0, l2_5])
+        st5 = hg.device_status(clear=False)[0]
+        st5 = max_over_ranks([float(st5)])[0]
+        rl5 = (fused_roofline(j5.Ml, C5_N, C5_K, world, ms5, peak) if world > 1 else
+               {"bound": "tensor", "achieved": 2.0 * C5_M * C5_N * C5_K / (ms5 * 1e-3) / 1e12,
+                "peak": peak, "unit": "TFLOP/s", "traffic": None})
+        if world == 1:
+            rl5["frac"] = rl5["achieved"] / peak
+        c5 = {"workload": f"gemm_{C5_M}x{C5_N}x{C5_K}_rowsharded{world}",
+              "baseline_config": "configs[4]", "scaling": "strong",
+              "M": C5_M, "N": C5_N, "K": C5_K, "rows_per_gpu": j5.Ml,
+              "steps": len(ev5), "warmup": 3, "ms_per_step": ms5,
+              "value": 2.0 * C5_M * C5_N * C5_K / (ms5 * 1e-3) / 1e12, "unit": "TFLOPS",
+              "roofline": rl5, "full_c_bit_identical_to_one_gpu_launch": chk5[0] == 0.0,
+              "full_c_rel_l2_vs_cublas_max_over_ranks": chk5[1], "device_status": int(st5),
+              "clocks": clk5.summary(),
+              "gpu_launches": len(ev5) * (1 if comm is None else 2)}
+        del j5, f5
+
     if comm is not None:
         hg.lib.hgemm_comm_destroy(comm)
 
     if rank == 0:
-        peak, hbm, src = peaks()
-        achieved = 2.0 * Ml * N * K / (kernel_ms * 1e-3) / 1e12
-        traffic = profiled_traffic(Ml, N, K)
         line = {
             "metric": "fp16_gemm_tflops", "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_ours,
@@ -586,37 +744,31 @@ def main():
             "scaling": "strong" if args.workload == "sharded32k" else "weak",
             "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (three_way.cu counter-hash fill, U[-1,1))",
-            "config": {"workload": (f"gemm_{M}x{N}x{K}" if world == 1 else
-                                    f"gemm_{M}x{N}x{K}_rowsharded_" +
-                                    ("peerstore" if args.exchange == "peer" else "allgather")),
-                       "exchange": None if world == 1 else (
-                           "fused GEMM epilogue stores every tile to all ranks' C over "
-                           "NVLink (16-byte stores, CUDA IPC peer mappings) + device flag barrier"
-                           if args.exchange == "peer" else
-                           f"NCCL all-gather / send-recv, {args.chunks} chunk(s)" +
-                           (f" (peer mapping unavailable: {peer_fallback})"
-                            if peer_fallback else "")),
+            "config": {"workload": main_workload, "exchange": exchange_desc,
                        "M": M, "N": N, "K": K, "alpha": 1.0, "beta": 0.0,
                        "rows_per_gpu": Ml, "parallelism": f"rowshard{world}",
                        "l2": "flushed (3x L2 memset) before every timed launch",
                        "timing": "CUDA events around each launch on the launching stream"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{src} bf16 dense (burst)"},
+            "roofline": roofline,
             "cublas": {"value": cub_value, "ms_per_step": ms_cub,
                        "paired_ratio_median": statistics.median(ratios) if ratios else None,
-                       "call": "cublasGemmEx(CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT)"},
+                       "call": "cublasGemmEx(CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT)",
+                       "note": None if world == 1 else
+                       "cuBLAS times this rank's local GEMM only (no exchange)"},
             "median_ms": statistics.median(t_ours),
             "region_ms_incl_flush_and_cublas": region_ms,
-            "check_rel_l2_vs_cublas": spot_l2,
-            "device_status": st_dev,
+            "full_c_bit_identical_to_one_gpu_launch": chk[0] == 0.0,
+            "full_c_rel_l2_vs_cublas_max_over_ranks": chk[1],
+            "check_rel_l2_vs_cublas": chk[1],
+            "device_status": int(st_max),
             "e2e": e2e,
             # our kernels per step: the GEMM; with the peer exchange also the one-warp
-            # barrier kernel; with NCCL one GEMM per chunk (NCCL's own kernels not counted)
-            "gpu_launches": args.steps * (1 if comm is None else
-                                          2 if args.exchange == "peer" else max(1, args.chunks)),
-            "clocks": clocks.summary(),
+            # exit barrier kernel; with NCCL one GEMM per chunk (NCCL's own kernels not counted)
+            "gpu_launches": gpu_launches,
+            "clocks": clk,
         }
+        if c5 is not None:
+            line["config5"] = c5
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(Ml, N, K)
         print(json.dumps(line), flush=True)

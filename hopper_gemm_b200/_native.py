@@ -59,6 +59,7 @@ SIGNATURES = {
     "hgemm_set_wait_timeout_ns": (None, [ctypes.c_ulonglong]),
     "hgemm_selftest_wait_timeout": (_i, [ctypes.c_ulonglong]),
     "hgemm_selftest_peer_barrier": (_i, [ctypes.c_ulonglong]),
+    "hgemm_selftest_peer_entry": (_i, [_i, ctypes.c_ulonglong]),
     "hgemm_release": (None, []),
     "hgemm_plan": (_i, [_i, _i, _i, _f, _i, _i, _i, _i, _i, _i, ctypes.POINTER(HgemmPlan)]),
     "hgemm_comm_unique_id": (_i, [_vp, ctypes.c_size_t]),

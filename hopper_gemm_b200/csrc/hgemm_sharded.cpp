@@ -11,10 +11,16 @@
 //
 // Fused path: once every rank has registered its C buffer (hgemm_comm_register_output, which
 // maps the peers' buffers into this process through CUDA IPC), hgemm_sharded_rank runs ONE
-// kernel per rank whose epilogue TMA-stores every finished C tile into the local C and into
-// each peer's C over NVLink, tile by tile while the math goes on, followed by a one-warp
-// barrier kernel that exchanges step epochs through flag arrays mapped the same way (release
-// stores / acquire loads at system scope, bounded waits). No NCCL call is made on this path.
+// kernel per rank whose epilogue TMA-stores every finished C tile into the local C and copies
+// it into each peer's C over NVLink with 16-byte stores, tile by tile while the math goes on.
+// Two epochs per step keep the ranks in order, both exchanged through flag arrays mapped the
+// same way (release stores / acquire loads at system scope, bounded waits):
+//   * entry: the kernel announces the step to every peer when it starts, and its epilogue
+//     stores into a peer's C only once that peer has announced the step too, i.e. once the
+//     peer's stream has passed everything queued before this step (its readers of C);
+//   * exit: a one-warp barrier kernel after the GEMM, so every rank's C is complete before
+//     anything queued after the call runs.
+// No NCCL call is made on this path.
 //
 // The reference (yz-wqf/Hopper_GEMM) is single-GPU and has no counterpart for this layer.
 // NCCL is resolved at run time from libnccl.so.2, so a process that already loaded NCCL
@@ -36,10 +42,17 @@
 extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_launch_unsplit(
     const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
     float alpha, float beta, hgemm_stream_t stream, int sm_limit);
-// Cross-GPU flag barrier (hgemm_sm100.cu; internal to this library).
+// Cross-GPU flag barrier, step exit (entry = 0) or entry (entry = 1) (hgemm_sm100.cu;
+// internal to this library).
 extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_peer_barrier(
     unsigned long long *const *flags, int rank, int nranks, unsigned long long epoch,
-    hgemm_stream_t stream);
+    int entry, hgemm_stream_t stream);
+// Peer-store GEMM gated on the peers' step-entry epochs (hgemm_sm100.cu; internal).
+extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_launch_peers_gated(
+    const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
+    float alpha, float beta, hgemm_stream_t stream, hgemm_half_t *const *peer_C, int npeers,
+    unsigned long long *const *post, const unsigned long long *const *wait,
+    unsigned long long epoch);
 
 namespace {
 
@@ -91,6 +104,9 @@ const NcclApi &nccl() {
 
 constexpr int kDefaultReservedSms = 16;
 constexpr int kMaxRanks = 8;  // the fused path stores to at most 7 peers
+// Each rank's flag array: [0, kMaxRanks) the last step each rank finished (exit epochs),
+// [kMaxRanks, 2 kMaxRanks) the last step each rank entered (entry epochs).
+constexpr int kFlagWords = 2 * kMaxRanks;
 
 // Start and size of the allocation that contains `p` (driver entry point, no -lcuda).
 bool allocation_range(const void *p, char **base, size_t *size) {
@@ -136,7 +152,7 @@ struct hgemm_comm_s {
   cudaEvent_t gather_done = nullptr;     // all exchanges finished (comm stream)
   // Fused path state.
   int *barrier_word = nullptr;              // device int for the registration all-reduce
-  unsigned long long *flags = nullptr;      // [kMaxRanks] step epochs announced by each rank
+  unsigned long long *flags = nullptr;      // [kFlagWords] step epochs announced by each rank
   unsigned long long epoch = 0;             // fused steps issued by this rank
   std::vector<void *> peer_flags_base;      // [nranks] IPC mappings of the peers' flags
   std::vector<unsigned long long *> peer_flags;
@@ -218,8 +234,8 @@ int hgemm_comm_init(hgemm_comm_t *out, int nranks, const void *id, size_t id_byt
       cudaEventCreateWithFlags(&c->gather_done, cudaEventDisableTiming) != cudaSuccess ||
       cudaMalloc(&c->barrier_word, sizeof(int)) != cudaSuccess ||
       cudaMalloc(&c->records_dev, sizeof(OutputRecord) * nranks) != cudaSuccess ||
-      cudaMalloc(&c->flags, sizeof(unsigned long long) * kMaxRanks) != cudaSuccess ||
-      cudaMemset(c->flags, 0, sizeof(unsigned long long) * kMaxRanks) != cudaSuccess ||
+      cudaMalloc(&c->flags, sizeof(unsigned long long) * kFlagWords) != cudaSuccess ||
+      cudaMemset(c->flags, 0, sizeof(unsigned long long) * kFlagWords) != cudaSuccess ||
       cudaMemset(c->barrier_word, 0, sizeof(int)) != cudaSuccess) {
     free_fused_state(c);
     a.CommDestroy(c->comm);
@@ -386,29 +402,47 @@ int hgemm_sharded_rank(hgemm_comm_t c, const hgemm_half_t *A_local, const hgemm_
   if (c->out_C && C == c->out_C && M % P == 0 && P > 1 &&
       static_cast<size_t>(M) * N * sizeof(hgemm_half_t) <= c->out_bytes) {
     // Fused path: one kernel computes this rank's rows and stores each tile into every
-    // peer's C as well; the barrier all-reduce follows whatever happened locally, so that
-    // the ranks' collective sequences stay the same.
+    // peer's C as well, gated on the peers' entry epochs; the exit barrier follows whatever
+    // happened locally, so that the ranks' flag sequences stay the same.
+    const unsigned long long ep = ++c->epoch;
     hgemm_half_t *peers[kMaxRanks];
+    unsigned long long *post[kMaxRanks];
+    const unsigned long long *wait[kMaxRanks];
     int n = 0;
-    for (int r = 0; r < P; ++r)
-      if (r != me) peers[n++] = c->peer_C[r] + static_cast<size_t>(rb) * row_elems;
+    for (int r = 0; r < P; ++r) {
+      if (r == me) continue;
+      peers[n] = c->peer_C[r] + static_cast<size_t>(rb) * row_elems;
+      post[n] = c->peer_flags[r] + kMaxRanks + me;  // peer r's entry flag for this rank
+      wait[n] = c->flags + kMaxRanks + r;            // this rank's entry flag for peer r
+      ++n;
+    }
     hgemm_half_t *Cl = C + static_cast<size_t>(rb) * row_elems;
     int st = HGEMM_OK;
+    bool entered = false;
     if (rc > 0) {
-      st = hgemm_launch_peers(A_local, B, Cl, rc, N, K, alpha, beta, stream, peers, n, 0);
+      st = hgemm_internal_launch_peers_gated(A_local, B, Cl, rc, N, K, alpha, beta, stream,
+                                             peers, n, post, wait, ep);
+      entered = st == HGEMM_OK;  // the kernel itself announced and waited for the entry
       if (st == HGEMM_ERR_NOT_FUSABLE) {
-        // Shapes without TMA stores: compute locally, then push the rows with copies.
+        // Shapes without TMA stores: compute locally, then an entry barrier (no peer may
+        // still be reading its C), then push the rows with copies.
         st = hgemm_internal_launch_unsplit(A_local, B, Cl, rc, N, K, alpha, beta, stream, 0);
+        const int est = hgemm_internal_peer_barrier(c->peer_flags.data(), me, P, ep, 1, stream);
+        entered = est == HGEMM_OK;
+        if (st == HGEMM_OK) st = est;
         for (int i = 0; i < n && st == HGEMM_OK; ++i)
           if (cudaMemcpyAsync(peers[i], Cl, static_cast<size_t>(rc) * row_elems * 2,
                               cudaMemcpyDeviceToDevice, s) != cudaSuccess)
             st = HGEMM_ERR_CUDA;
       }
     }
-    // Barrier: every rank announces the step in every peer's flag array and waits for
+    // A rank that launched no gated kernel still announces its entry, so that no peer's
+    // gate waits in vain.
+    if (!entered) hgemm_internal_peer_barrier(c->peer_flags.data(), me, P, ep, 1, stream);
+    // Exit barrier: every rank announces the step in every peer's flag array and waits for
     // theirs (a 1-warp kernel with bounded waits; its failures land in the device status
     // word). Posted whatever happened locally, so that no peer waits in vain.
-    const int bst = hgemm_internal_peer_barrier(c->peer_flags.data(), me, P, ++c->epoch, stream);
+    const int bst = hgemm_internal_peer_barrier(c->peer_flags.data(), me, P, ep, 0, stream);
     return st != HGEMM_OK ? st : bst;
   }
 

@@ -79,6 +79,7 @@ enum WaitSite : unsigned {
   kSiteClc = 9,
   kSitePeerBarrier = 10,
   kSiteSplitReduce = 11,
+  kSitePeerEntry = 12,
 };
 __device__ unsigned int g_dev_status = 0;
 
@@ -138,9 +139,21 @@ struct KParams {
 // row-sharded GEMM delivers its rows to every rank while it computes them (the SM's TMA
 // unit only carries the local C and the operand loads; a TMA-store variant of the copy
 // measured the same on 4 B200s).
+//
+// Step-entry gate (epoch != 0): a destination may still be reading its C from the previous
+// step when this kernel starts. Every CTA therefore first announces `epoch` in each
+// destination's entry flag for this rank (post[d], a system-scope release store: the
+// kernel has started, so everything queued before it on this stream, including this
+// rank's own readers of C, has finished), and each epilogue warp, before its first peer
+// store, waits until every destination has announced the same epoch here (wait[d],
+// acquire loads, bounded by the wait timeout). A wait that runs out records
+// kSitePeerEntry in the device status word and the kernel keeps going without peer stores.
 constexpr int kMaxPeers = 7;
 struct PeerMaps {
   __half *ptr[kMaxPeers];
+  unsigned long long *post[kMaxPeers];        // destination d's entry flag for this rank
+  const unsigned long long *wait[kMaxPeers];  // this rank's entry flag for destination d
+  unsigned long long epoch;                   // 0: no gate (the caller orders the readers)
   int n;
 };
 // C stores carry an L2 evict-first policy from this K on: with long main loops the A and B
@@ -705,6 +718,32 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
     const uint32_t tempty_leader =
         (PAIR == 2) ? ptx::mapa(ptx::smem_u32(&tempty[0]), 0u) : ptx::smem_u32(&tempty[0]);
     const float alpha = p.alpha, beta = p.beta;
+    // Step-entry gate of the peer stores (see PeerMaps). Announced by one thread per CTA;
+    // each warp waits once, here, while the first tile's main loop runs.
+    int npeer_live = npeer;
+    if (PEERS && npeer > 0 && peers.epoch != 0) {
+      if (ew == 0 && lane == 0)
+        for (int d = 0; d < npeer; ++d) ptx::st_release_sys_u64(peers.post[d], peers.epoch);
+      int okp = 1;
+      if (lane == 0) {
+        const uint64_t t0 = ptx::globaltimer();
+        for (int d = 0; d < npeer && okp; ++d) {
+          for (uint32_t n = 0;; ++n) {
+            if (ptx::ld_acquire_sys_u64(peers.wait[d]) >= peers.epoch) break;
+            if ((n & 15u) == 15u &&
+                (*abort_flag || ptx::globaltimer() - t0 > p.timeout_ns)) {
+              atomicCAS(&g_dev_status, 0u, kDevTimeout | kSitePeerEntry);
+              okp = 0;
+              break;
+            }
+            ptx::nanosleep_ns(128);
+          }
+        }
+      }
+      okp = __shfl_sync(0xffffffffu, okp, 0);
+      __syncwarp();
+      if (!okp) npeer_live = 0;  // this rank's tiles stay local; the status word says why
+    }
     int it = 0;
     int chunk_ctr = 0;
     int sslot = 0;
@@ -731,7 +770,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
         const uint4 v = *reinterpret_cast<const uint4 *>(stgp + sw128_off(rr, jj));
         if (gr < p.M && gc < p.N) {
           const size_t off = static_cast<size_t>(gr) * p.N + gc;
-          for (int d = 0; d < npeer; ++d) {
+          for (int d = 0; d < npeer_live; ++d) {
             if (p.c_evict_first)
               ptx::st_global_v4_hint(peers.ptr[d] + off, v, c_policy);
             else
@@ -1002,7 +1041,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
                 }
                 ptx::bulk_commit_group();
               }
-              if (npeer > 0) push_peers(stg0 + buf, row0, ccol);
+              if (npeer_live > 0) push_peers(stg0 + buf, row0, ccol);
             }
           }
           if (aborted) break;
@@ -1137,7 +1176,7 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
             }
             ptx::bulk_commit_group();  // one group per chunk, empty when nothing was stored
           }
-          if (npeer > 0) push_peers(stg, row0, ccol);
+          if (npeer_live > 0) push_peers(stg, row0, ccol);
         } else {
           // C's rows are not 16-byte aligned: stage through smem, then coalesced 2-byte
           // accesses (lanes along a row), predicated on the M/N edges.
@@ -1318,32 +1357,33 @@ __global__ void wait_selftest_kernel(unsigned long long timeout_ns, int *out) {
   }
 }
 
-// Cross-GPU barrier of a row-sharded step. Every rank owns an array of kMaxRanksBarrier
-// 64-bit epochs; flags[r] in rank q's array is the last step that rank r has finished (its
-// GEMM kernel, whose peer stores were completed and fenced system-wide, precedes this
-// kernel in the stream). Lane i announces the step to rank i (release store, system
-// scope, through the CUDA IPC mapping of rank i's array), then waits until rank i has
-// announced it here (acquire load), at most timeout_ns; a wait that runs out records
-// kSitePeerBarrier in the device status word and returns.
+// Cross-GPU barrier of a row-sharded step. Every rank owns an array of 2 x kMaxRanksBarrier
+// 64-bit epochs: slot r is the last step that rank r has finished (its GEMM kernel, whose
+// peer stores were completed and fenced system-wide, precedes this kernel in the stream),
+// slot kMaxRanksBarrier + r the last step that rank r has entered (see PeerMaps). Lane i
+// announces the epoch to rank i (release store, system scope, through the CUDA IPC mapping
+// of rank i's array), then waits until rank i has announced it here (acquire load), at
+// most timeout_ns; a wait that runs out records its site in the device status word and
+// returns.
 constexpr int kMaxRanksBarrier = 8;
+static_assert(kMaxPeers + 1 == kMaxRanksBarrier, "one flag slot per rank");
 struct BarrierArgs {
   unsigned long long *flags[kMaxRanksBarrier];  // rank i's flag array as mapped here
   int rank, nranks;
+  int slot_base;  // 0: step-exit epochs; kMaxRanksBarrier: step-entry epochs
 };
 __global__ void peer_barrier_kernel(const BarrierArgs a, unsigned long long epoch,
                                     unsigned long long timeout_ns) {
   const int i = threadIdx.x;
   if (i >= a.nranks || i == a.rank) return;
-  unsigned long long *remote = a.flags[i] + a.rank;
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(remote), "l"(epoch) : "memory");
-  const unsigned long long *mine = a.flags[a.rank] + i;
+  ptx::st_release_sys_u64(a.flags[i] + a.slot_base + a.rank, epoch);
+  const unsigned long long *mine = a.flags[a.rank] + a.slot_base + i;
   const unsigned long long t0 = ptx::globaltimer();
   for (unsigned it = 0;; ++it) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
-    if (v >= epoch) return;
+    if (ptx::ld_acquire_sys_u64(mine) >= epoch) return;
     if ((it & 15u) == 15u && ptx::globaltimer() - t0 > timeout_ns) {
-      atomicCAS(&g_dev_status, 0u, kDevTimeout | kSitePeerBarrier);
+      atomicCAS(&g_dev_status, 0u,
+                kDevTimeout | (a.slot_base ? kSitePeerEntry : kSitePeerBarrier));
       return;
     }
     ptx::nanosleep_ns(64);
@@ -1765,11 +1805,19 @@ int launch_simt(const __half *A, const __half *B, __half *C, int M, int N, int K
   return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
 }
 
+// Step-entry gate of a peer-store launch (PeerMaps): per destination, where this rank posts
+// its entry epoch and where that destination posts its own.
+struct PeerGate {
+  unsigned long long *const *post;
+  const unsigned long long *const *wait;
+  unsigned long long epoch;
+};
+
 // Launch the tcgen05 kernel for an already-made plan on operands with 16-byte strides.
 int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const __half *B,
               int ldb, __half *C, int M, int N, int K, float alpha, float beta,
               cudaStream_t stream, DevState &d, __half *const *peer_C = nullptr,
-              int npeers = 0) {
+              int npeers = 0, const PeerGate *gate = nullptr) {
   const TileInfo &ti = kTiles[tile];
   const bool tma_epi = pl.tma_store != 0;
   CUtensorMap ta, tb, tc;
@@ -1788,7 +1836,14 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
       if (!peer_C[i] || reinterpret_cast<uintptr_t>(peer_C[i]) % 16 != 0)
         return HGEMM_ERR_NOT_FUSABLE;
       peers.ptr[i] = peer_C[i];
+      if (gate && gate->epoch != 0) {
+        if (!gate->post || !gate->wait || !gate->post[i] || !gate->wait[i])
+          return HGEMM_ERR_INVALID_ARG;
+        peers.post[i] = gate->post[i];
+        peers.wait[i] = gate->wait[i];
+      }
     }
+    peers.epoch = gate ? gate->epoch : 0ull;
     peers.n = npeers;
   }
   const int flav = !tma_epi ? kFlavSimt
@@ -1858,7 +1913,8 @@ int launch_compact(const __half *src, __half *dst, int rows, int cols, int ld, i
 // C); every element the GEMM reads from it is written earlier on the same stream.
 int launch_padded(const hgemm_plan_t &pl, const __half *A, const __half *B, __half *C, int M,
                   int N, int K, float alpha, float beta, cudaStream_t stream, DevState &d,
-                  __half *w, __half *const *peer_C, int npeers) {
+                  __half *w, __half *const *peer_C, int npeers,
+                  const PeerGate *gate = nullptr) {
   int st = HGEMM_OK;
   const __half *Ause = A, *Buse = B;
   __half *Cuse = C;
@@ -1885,7 +1941,7 @@ int launch_padded(const hgemm_plan_t &pl, const __half *A, const __half *B, __ha
   for (int t = 0; t < kNumTiles; ++t)
     if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;
   st = launch_tc(pl, tile, Ause, pl.lda, Buse, pl.ldb, Cuse, M, N, K, alpha, beta, stream, d,
-                 peer_C, npeers);
+                 peer_C, npeers, gate);
   if (st != HGEMM_OK || !pl.pad_c) return st;
   return launch_compact(Cuse, C, M, N, pl.ldc, d.sm_count, stream);
 }
@@ -1893,7 +1949,7 @@ int launch_padded(const hgemm_plan_t &pl, const __half *A, const __half *B, __ha
 int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K, float alpha,
                 float beta, cudaStream_t stream, int force_bm, int force_bn, int group_m,
                 int sm_limit = 0, __half *const *peer_C = nullptr, int npeers = 0,
-                int ksplit_req = 0) {
+                int ksplit_req = 0, const PeerGate *gate = nullptr) {
   if (M < 0 || N < 0 || K < 0) return HGEMM_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return HGEMM_OK;
   if (!A || !B || !C) return HGEMM_ERR_INVALID_ARG;
@@ -1935,7 +1991,7 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
     w = static_cast<__half *>(scratch_get(*d, pl.scratch_bytes));
     if (!w) return HGEMM_ERR_ALLOC;
   }
-  return launch_padded(pl, A, B, C, M, N, K, alpha, beta, stream, *d, w, peer_C, npeers);
+  return launch_padded(pl, A, B, C, M, N, K, alpha, beta, stream, *d, w, peer_C, npeers, gate);
 }
 
 // ---------------------------------------------------------------- autotune cache
@@ -1943,6 +1999,10 @@ struct TuneCfg {
   int bm, bn, group_m;
 };
 std::map<std::tuple<int, int, int, int>, TuneCfg> g_tune;
+
+// Forgets the cached device addresses of the no-allocation scratch array (defined with
+// hgemm_launch_noalloc below), so that they are looked up again after a device reset.
+void noalloc_forget_addresses();
 
 }  // namespace
 }  // namespace hgemm
@@ -1970,10 +2030,11 @@ __attribute__((visibility("hidden"))) int hgemm_internal_launch_unsplit(
                                 sm_limit > 0 ? sm_limit : 0, nullptr, 0, 1));
 }
 
-// Used by the multi-GPU layer only (not part of the public header).
+// Used by the multi-GPU layer only (not part of the public header). entry = 0: step-exit
+// barrier; entry = 1: step-entry barrier (every rank has entered the step).
 __attribute__((visibility("hidden"))) int hgemm_internal_peer_barrier(
     unsigned long long *const *flags, int rank, int nranks, unsigned long long epoch,
-    hgemm_stream_t stream) {
+    int entry, hgemm_stream_t stream) {
   if (!flags || nranks < 1 || nranks > kMaxRanksBarrier || rank < 0 || rank >= nranks)
     return HGEMM_ERR_INVALID_ARG;
   BarrierArgs a;
@@ -1981,9 +2042,26 @@ __attribute__((visibility("hidden"))) int hgemm_internal_peer_barrier(
   for (int r = 0; r < nranks; ++r) a.flags[r] = flags[r];
   a.rank = rank;
   a.nranks = nranks;
+  a.slot_base = entry ? kMaxRanksBarrier : 0;
   peer_barrier_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       a, epoch, g_timeout_ns.load());
   return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
+}
+
+// Peer-store GEMM with the step-entry gate (PeerMaps) for the multi-GPU layer (not part of
+// the public header): post[d] / wait[d] are destination d's entry flag for this rank and this
+// rank's entry flag for destination d; epoch > 0.
+__attribute__((visibility("hidden"))) int hgemm_internal_launch_peers_gated(
+    const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
+    float alpha, float beta, hgemm_stream_t stream, hgemm_half_t *const *peer_C, int npeers,
+    unsigned long long *const *post, const unsigned long long *const *wait,
+    unsigned long long epoch) {
+  if (npeers < 1 || npeers > kMaxPeers || !peer_C || !post || !wait || epoch == 0)
+    return set_status(HGEMM_ERR_INVALID_ARG);
+  const PeerGate gate{post, wait, epoch};
+  return set_status(launch_impl(A, B, C, M, N, K, alpha, beta,
+                                reinterpret_cast<cudaStream_t>(stream), 0, 0, 0, 0, peer_C,
+                                npeers, 0, &gate));
 }
 
 int hgemm_launch_peers(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
@@ -2152,23 +2230,24 @@ int hgemm_selftest_peer_barrier(unsigned long long timeout_ns) {
   // Rank 0 of a two-rank barrier whose partner never announces: the bounded wait must run
   // out, record kSitePeerBarrier and return. Both flag arrays are local memory.
   unsigned long long *d = nullptr;
-  if (cudaMalloc(&d, 2 * kMaxRanksBarrier * sizeof(unsigned long long)) != cudaSuccess)
+  if (cudaMalloc(&d, 4 * kMaxRanksBarrier * sizeof(unsigned long long)) != cudaSuccess)
     return set_status(HGEMM_ERR_CUDA);
-  int st = cudaMemset(d, 0, 2 * kMaxRanksBarrier * sizeof(unsigned long long)) == cudaSuccess
+  int st = cudaMemset(d, 0, 4 * kMaxRanksBarrier * sizeof(unsigned long long)) == cudaSuccess
                ? HGEMM_OK
                : HGEMM_ERR_CUDA;
   if (st == HGEMM_OK) {
     BarrierArgs a;
     std::memset(&a, 0, sizeof(a));
     a.flags[0] = d;
-    a.flags[1] = d + kMaxRanksBarrier;
+    a.flags[1] = d + 2 * kMaxRanksBarrier;
     a.rank = 0;
     a.nranks = 2;
+    a.slot_base = 0;
     peer_barrier_kernel<<<1, 32>>>(a, 1ull, timeout_ns);
     st = cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
     unsigned long long announced = 0;
     if (st == HGEMM_OK &&
-        cudaMemcpy(&announced, d + kMaxRanksBarrier, sizeof(announced),
+        cudaMemcpy(&announced, d + 2 * kMaxRanksBarrier, sizeof(announced),
                    cudaMemcpyDeviceToHost) != cudaSuccess)
       st = HGEMM_ERR_CUDA;
     if (st == HGEMM_OK && announced != 1ull) st = HGEMM_ERR_CUDA;  // lane 1 must have announced
@@ -2179,6 +2258,64 @@ int hgemm_selftest_peer_barrier(unsigned long long timeout_ns) {
   if (st != HGEMM_OK) return set_status(st);
   set_status(HGEMM_OK);
   return (dev == HGEMM_ERR_DEVICE_TIMEOUT && where == static_cast<int>(kSitePeerBarrier))
+             ? HGEMM_ERR_DEVICE_TIMEOUT
+             : HGEMM_OK;
+}
+
+int hgemm_selftest_peer_entry(int satisfied, unsigned long long timeout_ns) {
+  // A 256 x 256 x 64 GEMM of zeros through the gated peer-store kernel, on one GPU with local
+  // memory only: its one "peer" C is a local buffer pre-filled with 0x5A bytes and its entry
+  // flag is either already at the step's epoch (satisfied) or never set.
+  constexpr int M = 256, N = 256, K = 64;
+  const size_t nA = static_cast<size_t>(M) * K, nB = static_cast<size_t>(K) * N,
+               nC = static_cast<size_t>(M) * N;
+  const size_t bytes = (nA + nB + 2 * nC) * sizeof(__half) + 2 * sizeof(unsigned long long);
+  char *buf = nullptr;
+  if (cudaMalloc(&buf, bytes) != cudaSuccess) return set_status(HGEMM_ERR_CUDA);
+  __half *A = reinterpret_cast<__half *>(buf), *B = A + nA, *C = B + nB, *P = C + nC;
+  unsigned long long *flags = reinterpret_cast<unsigned long long *>(P + nC);
+  const unsigned long long epoch = 1, want = satisfied ? epoch : 0;
+  int st = (cudaMemset(A, 0, (nA + nB) * sizeof(__half)) == cudaSuccess &&
+            cudaMemset(C, 0xFF, nC * sizeof(__half)) == cudaSuccess &&
+            cudaMemset(P, 0x5A, nC * sizeof(__half)) == cudaSuccess &&
+            cudaMemset(flags, 0, sizeof(unsigned long long)) == cudaSuccess &&
+            cudaMemcpy(flags + 1, &want, sizeof(want), cudaMemcpyHostToDevice) == cudaSuccess)
+               ? HGEMM_OK
+               : HGEMM_ERR_CUDA;
+  const unsigned long long saved = g_timeout_ns.load();
+  if (st == HGEMM_OK) {
+    g_timeout_ns.store(timeout_ns ? timeout_ns : 1ull);
+    __half *peer[1] = {P};
+    unsigned long long *post[1] = {flags};
+    const unsigned long long *wait[1] = {flags + 1};
+    const PeerGate gate{post, wait, epoch};
+    st = launch_impl(A, B, C, M, N, K, 1.0f, 0.0f, 0, 0, 0, 0, 0, peer, 1, 0, &gate);
+    if (cudaDeviceSynchronize() != cudaSuccess && st == HGEMM_OK) st = HGEMM_ERR_CUDA;
+    g_timeout_ns.store(saved);
+  }
+  int where = 0;
+  const int dev = hgemm_device_status(1, &where);  // read and clear what the kernel recorded
+  std::vector<uint16_t> hc(nC), hp(nC);
+  unsigned long long posted = 0;
+  if (st == HGEMM_OK &&
+      (cudaMemcpy(hc.data(), C, nC * sizeof(__half), cudaMemcpyDeviceToHost) != cudaSuccess ||
+       cudaMemcpy(hp.data(), P, nC * sizeof(__half), cudaMemcpyDeviceToHost) != cudaSuccess ||
+       cudaMemcpy(&posted, flags, sizeof(posted), cudaMemcpyDeviceToHost) != cudaSuccess))
+    st = HGEMM_ERR_CUDA;
+  cudaFree(buf);
+  if (st != HGEMM_OK) return set_status(st);
+  set_status(HGEMM_OK);
+  // The local C is computed either way and the kernel announced its own entry.
+  bool good = posted == epoch;
+  for (size_t i = 0; i < nC && good; ++i) good = hc[i] == 0;
+  if (satisfied) {
+    for (size_t i = 0; i < nC && good; ++i) good = hp[i] == 0;
+    if (!good) return HGEMM_ERR_CUDA;
+    return dev;  // HGEMM_OK: no wait ran out
+  }
+  for (size_t i = 0; i < nC && good; ++i) good = hp[i] == 0x5A5Au;
+  if (!good) return HGEMM_ERR_CUDA;
+  return (dev == HGEMM_ERR_DEVICE_TIMEOUT && where == static_cast<int>(kSitePeerEntry))
              ? HGEMM_ERR_DEVICE_TIMEOUT
              : HGEMM_OK;
 }
@@ -2197,6 +2334,7 @@ void hgemm_release(void) {
   }
   cudaSetDevice(cur);
   g_tune.clear();
+  noalloc_forget_addresses();
 }
 
 int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int force_bn,
@@ -2214,9 +2352,12 @@ int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int
 // caller-facing path must not take the allocator's lock or implicitly synchronise the
 // device (cudaMalloc/cudaFree may do both), or code with a strict memory budget decided
 // ahead of time. hgemm_launch_noalloc serves them: it is hgemm_launch, except that the one
-// scratch buffer the path can need -- the restrided copy of A when K % 8 != 0 and of B when
-// N % 8 != 0 -- lives in the fixed-size array below, which the library's module owns on
-// every device that loads it (until the process exits), instead of coming from cudaMalloc.
+// scratch buffer the path can need -- the restrided copy of A when K % 8 != 0, of B when
+// N % 8 != 0, and the 16-byte-strided copy of C when N % 8 != 0 and beta != 0 -- lives in the
+// fixed-size array below, which the library's module owns on every device that loads it
+// (until the process exits), instead of coming from cudaMalloc. The array's device address
+// is looked up once per device and cached; hgemm_release() forgets the cached addresses (call
+// it after a device reset, which reloads the module).
 namespace hgemm {
 namespace {
 
@@ -2229,6 +2370,11 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratch
 
 std::mutex g_noalloc_mu;
 void *g_noalloc_ptr[64] = {};
+
+void noalloc_forget_addresses() {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  for (void *&p : g_noalloc_ptr) p = nullptr;
+}
 
 // Caller holds g_noalloc_mu; `dev` is current.
 int noalloc_scratch(int dev, __half **out) {

@@ -7,9 +7,14 @@ ncclAllGather for equal blocks, grouped send/recv otherwise or when the local ro
 into chunks whose exchange overlaps the next chunk's GEMM).
 
 register_output(C) switches a communicator to the fused path for that output buffer: the
-peers' C buffers are mapped into every process (CUDA IPC) and a single kernel per rank stores
-each finished tile into every rank's C over NVLink while it computes, so the exchange
-overlaps the math tile by tile; a 4-byte NCCL all-reduce is the only collective per call.
+peers' C buffers and step-flag arrays are mapped into every process (CUDA IPC) and a single
+kernel per rank stores each finished tile into every rank's C over NVLink while it computes,
+so the exchange overlaps the math tile by tile. No NCCL call is made per step: the kernel
+stores into a peer's C only once that peer's stream has entered the same step (an entry
+epoch each rank's kernel announces when it starts), and a one-warp barrier kernel after it
+waits until every rank has finished the step (an exit epoch); both are release/acquire flags
+at system scope with bounded waits, failures recorded in the device status word. Readers of
+C must therefore be ordered on the stream passed to each call (or before it).
 
 torch.distributed (any backend) is used only for the rendezvous: rank 0 creates the NCCL id
 and broadcasts it; the library then owns its own NCCL communicator. The reference

@@ -79,12 +79,15 @@ int hgemm_launch_tuned(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_
  * that must not allocate device memory at call time -- a framework that owns a fixed
  * device-memory pool and forbids other cudaMalloc calls, or a latency-critical path that
  * cannot take the allocator's lock or its implicit device synchronisation. The only scratch
- * the GEMM can need (the restrided copy of A when K % 8 != 0 and of B when N % 8 != 0) comes
- * from a fixed array of hgemm_noalloc_scratch_bytes() (64 MiB) that the library keeps on every
- * device that loads it, until the process exits; no cudaMalloc/cudaFree happens here.
- * Shapes whose restrided operands need more return HGEMM_ERR_TOO_LARGE before any work.
+ * the GEMM can need (the restrided copy of A when K % 8 != 0, of B when N % 8 != 0, and the
+ * 16-byte-strided copy of C when N % 8 != 0 and beta != 0) comes from a fixed array of
+ * hgemm_noalloc_scratch_bytes() (64 MiB) that the library keeps on every device that loads
+ * it, until the process exits; no cudaMalloc/cudaFree happens here. Shapes whose copies need
+ * more in total (e.g. M x N above 32 Mi elements when only C needs the copy) return
+ * HGEMM_ERR_TOO_LARGE before any work.
  * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call outside any stream capture. Each device has
+ * (cudaGetSymbolAddress); make that first call outside any stream capture, and call
+ * hgemm_release() after a device reset so that the address is looked up again. Each device has
  * its own copy of the array, and every call on a device shares that copy and leaves its
  * contents behind: two calls on one device that can overlap on the GPU (different streams)
  * race on it when both need restriding, so order them. Same arguments, semantics and status
@@ -118,7 +121,19 @@ int hgemm_selftest_wait_timeout(unsigned long long timeout_ns);
  * (the expected outcome), HGEMM_OK if it did not. Clears the device status word. */
 int hgemm_selftest_peer_barrier(unsigned long long timeout_ns);
 
-/* Frees the per-device scratch used to restride A (K % 8 != 0) or B (N % 8 != 0). */
+/* Multi-GPU step-entry gate self-test (one GPU, local memory only): runs the gated
+ * peer-store kernel of hgemm_sharded_rank's fused path on a 256 x 256 x 64 GEMM whose one
+ * "peer" C is a local buffer. satisfied != 0: the peer's entry flag is already set, and the
+ * call returns HGEMM_OK when the peer copy was written and equals C. satisfied == 0: the
+ * flag is never set; the call returns HGEMM_ERR_DEVICE_TIMEOUT when the gate gave up after
+ * ~timeout_ns, recorded its site, left the peer copy untouched and still wrote the local C
+ * (the expected outcome). Any other result means the gate misbehaved. Clears the device
+ * status word. No counterpart in the reference. */
+int hgemm_selftest_peer_entry(int satisfied, unsigned long long timeout_ns);
+
+/* Frees the per-device scratch used to restride A (K % 8 != 0), B (N % 8 != 0) or C
+ * (N % 8 != 0 with beta != 0), drops the autotuner's cache and forgets the cached device
+ * addresses of hgemm_launch_noalloc's array. */
 void hgemm_release(void);
 
 /* Like hgemm_launch, but the GEMM runs on at most `sm_limit` SMs (persistent CTAs with a
@@ -130,9 +145,12 @@ int hgemm_launch_sm_limit(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_ha
 
 /* Like hgemm_launch_sm_limit (sm_limit <= 0: every SM), and every C tile is also written
  * into `npeers` (<= 7) other M x N row-major buffers, such as the C buffers of peer GPUs
- * mapped into this process: the epilogue issues one more TMA store per destination. The
- * peer buffers are written asynchronously from the kernel; the caller orders their readers
- * after it (hgemm_sharded_rank does so with a collective barrier). Returns
+ * mapped into this process: after the local TMA store of each 32 x 64 chunk, the epilogue
+ * copies the staged chunk to every destination with 16-byte stores. The peer buffers are
+ * written asynchronously from the kernel and nothing here orders them against the
+ * destinations' own work: the caller must make sure that no destination reads or writes its
+ * buffer while this kernel may store into it, before and after. hgemm_sharded_rank's fused
+ * path does that with step-entry and step-exit flags exchanged between the ranks. Returns
  * HGEMM_ERR_NOT_FUSABLE without launching when the shape takes a path without TMA stores.
  * No counterpart in the reference. */
 int hgemm_launch_peers(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
@@ -183,8 +201,10 @@ int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int
 /* ---------------------------------------------------------------- multi-GPU (row shards)
  * One process per GPU. Rank r owns rows [row_begin(r), row_begin(r+1)) of A and C, with
  * row_begin(r) = (M * r) / nranks; B is replicated. hgemm_sharded_rank computes the local
- * C row block with the GEMM above and all-gathers C in place over NCCL, so every rank ends
- * with the full C. The reference is single-GPU; this layer has no counterpart there.
+ * C row block with the GEMM above and gathers C in place (NCCL, or the fused peer-store
+ * path once the output is registered), so every rank ends with the full C. The reference
+ * is single-GPU; this layer has no counterpart there (the survey's single-process
+ * hgemm_sharded(ngpu, devs, ...) is served by one call of hgemm_sharded_rank per process).
  * NCCL is loaded at run time (libnccl.so.2); without it these return HGEMM_ERR_NCCL. */
 typedef struct hgemm_comm_s *hgemm_comm_t;
 
@@ -194,12 +214,19 @@ int hgemm_comm_destroy(hgemm_comm_t comm);
 
 /* Collective (every rank calls it): registers this rank's full M x N output buffer C
  * (`bytes` long, 16-byte aligned, from cudaMalloc) and maps every peer's registered buffer
- * into this process through CUDA IPC. While registered, hgemm_sharded_rank called with that
- * buffer (on every rank) and M % nranks == 0 runs the fused path: one kernel per rank that
- * stores each finished tile into all ranks' C over NVLink, then a 4-byte barrier
- * all-reduce; no NCCL kernel moves C. C == NULL, bytes == 0 unregisters. Returns HGEMM_OK
- * only when every rank registered (the outcome is agreed on collectively). No counterpart
- * in the reference. */
+ * and step-flag array into this process through CUDA IPC. While registered,
+ * hgemm_sharded_rank called with that buffer (on every rank) and M % nranks == 0 runs the
+ * fused path: one kernel per rank that stores each finished tile into all ranks' C over
+ * NVLink, then a one-warp barrier kernel; no NCCL kernel moves C and no NCCL call is made
+ * per step. Ordering between steps uses two epochs in flag arrays (release stores /
+ * acquire loads at system scope, every wait bounded by hgemm_set_wait_timeout_ns, a wait
+ * that runs out recorded in the device status word): the kernel stores into a peer's C only
+ * after that peer's stream has entered the same step (so the peer's readers of its C, queued
+ * before the call on the stream passed to hgemm_sharded_rank, have finished), and the
+ * barrier kernel returns only when every rank has finished the step (so readers queued
+ * after the call see the whole C). C == NULL, bytes == 0 unregisters. Returns HGEMM_OK only
+ * when every rank registered (the outcome is agreed on collectively). No counterpart in the
+ * reference. */
 int hgemm_comm_register_output(hgemm_comm_t comm, hgemm_half_t *C, size_t bytes);
 
 /* Address, in this process, of rank r's registered output buffer (this rank's own C for

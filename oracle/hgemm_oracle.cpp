@@ -8,8 +8,9 @@
 //       r   = (double)alpha * acc + (double)beta * (double)C_in[i][j]
 //     Products of two fp16 values are exact in fp64, and every (i, j) sum is accumulated in
 //     the same k order as the reference's triple loop, so the results are bit-identical to
-//     that loop; only the loop nest is reordered (k outer, j inner) for cache locality, and
-//     rows are spread over std::thread workers.
+//     that loop; only the loop nest is reordered (blocks of rows and columns, k running
+//     over all of K inside each block) for cache locality, and the blocks are spread over
+//     std::thread workers.
 //   * oracle_mt_*: the harnesses' seeded inputs -- std::mt19937(seed) with
 //     std::uniform_real_distribution<float>(lo, hi) (check_all.cu:14, check_fp64.cu:16,
 //     check_large.cu:15), each draw rounded to half by round-to-nearest-even
@@ -135,31 +136,58 @@ void oracle_f32_to_f16_array(const float *src, uint16_t *dst, size_t n) {
   for (size_t i = 0; i < n; ++i) dst[i] = f32_to_f16(src[i]);
 }
 
+// Inner update of one accumulator row over `n` columns: ac[j] += a * b[j], one product and
+// one addition per element (no fused multiply-add: the library is built with
+// -ffp-contract=off), so every element is summed exactly as the reference's loop sums it.
+// Cloned for AVX2 and a baseline x86-64 target; the loader picks the one the CPU runs.
+__attribute__((target_clones("avx2", "default"))) void axpy_row(double *ac, double a,
+                                                               const float *b, int n) {
+  for (int j = 0; j < n; ++j) ac[j] += a * static_cast<double>(b[j]);
+}
+
 // out[(r)*N + j] for the `nrows` rows listed in `rows` (any order, any subset).
 // Cin may be null when beta == 0 (the reference never reads C then).
+// B is widened to fp32 once (every binary16 value is exactly a float, and exactly the
+// double it converts to); the work is split into tasks of up to kRowBlock rows x kColBlock
+// columns whose accumulators stay in cache while k runs over all of K in increasing order.
 void oracle_gemm_f64_rows(const uint16_t *A, const uint16_t *B, const uint16_t *Cin, double *out,
                           int M, int N, int K, double alpha, double beta, const int *rows,
                           int nrows, int nthreads) {
   (void)M;
+  constexpr int kRowBlock = 8, kColBlock = 512;
   const double *lut = half_lut();
-  const int nw = std::max(1, std::min(resolve_threads(nthreads), nrows));
-  std::vector<std::vector<double>> acc_w(nw, std::vector<double>(N)), arow_w(nw, std::vector<double>(K));
-  parallel_for(nrows, nw, 1, [&](int w, int t) {
-    std::vector<double> &acc = acc_w[w];
-    std::vector<double> &arow = arow_w[w];
-    const int i = rows[t];
-    widen(A + static_cast<size_t>(i) * K, arow.data(), K);
-    std::fill(acc.begin(), acc.end(), 0.0);
+  std::vector<float> Bf(static_cast<size_t>(K) * N);
+  parallel_for(K, nthreads, 16, [&](int, int k) {
+    const uint16_t *b = B + static_cast<size_t>(k) * N;
+    float *d = Bf.data() + static_cast<size_t>(k) * N;
+    for (int j = 0; j < N; ++j) d[j] = static_cast<float>(lut[b[j]]);
+  });
+  const int nrb = (nrows + kRowBlock - 1) / kRowBlock;
+  const int njt = (N + kColBlock - 1) / kColBlock;
+  const int ntask = nrb * njt;
+  const int nw = std::max(1, std::min(resolve_threads(nthreads), ntask));
+  std::vector<std::vector<double>> acc_w(nw, std::vector<double>(kRowBlock * kColBlock));
+  parallel_for(ntask, nw, 1, [&](int w, int task) {
+    const int rbi = task / njt, jt = task % njt;
+    const int t0 = rbi * kRowBlock, t1 = std::min(nrows, t0 + kRowBlock);
+    const int j0 = jt * kColBlock, jw = std::min(N, j0 + kColBlock) - j0;
+    double *acc = acc_w[w].data();
+    std::fill(acc, acc + kRowBlock * kColBlock, 0.0);
     for (int k = 0; k < K; ++k) {
-      const double a = arow[k];
-      const uint16_t *b = B + static_cast<size_t>(k) * N;
-      for (int j = 0; j < N; ++j) acc[j] += a * lut[b[j]];
+      const float *bk = Bf.data() + static_cast<size_t>(k) * N + j0;
+      for (int t = t0; t < t1; ++t)
+        axpy_row(acc + (t - t0) * kColBlock, lut[A[static_cast<size_t>(rows[t]) * K + k]], bk, jw);
     }
-    double *o = out + static_cast<size_t>(t) * N;
-    for (int j = 0; j < N; ++j) {
-      double r = alpha * acc[j];
-      if (beta != 0.0) r += beta * static_cast<double>(f16_to_f32(Cin[static_cast<size_t>(i) * N + j]));
-      o[j] = r;
+    for (int t = t0; t < t1; ++t) {
+      const int i = rows[t];
+      const double *ac = acc + (t - t0) * kColBlock;
+      double *o = out + static_cast<size_t>(t) * N + j0;
+      for (int j = 0; j < jw; ++j) {
+        double r = alpha * ac[j];
+        if (beta != 0.0)
+          r += beta * static_cast<double>(f16_to_f32(Cin[static_cast<size_t>(i) * N + j0 + j]));
+        o[j] = r;
+      }
     }
   });
 }

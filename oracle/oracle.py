@@ -28,6 +28,19 @@ def build(force=False):
     return LIB_PATH
 
 
+def build_ref():
+    """Builds the reference's own correctness harnesses against this repository's GEMM library
+    (oracle/_ref/, see oracle/Makefile `ref`). Needs the reference checkout; where it is absent
+    (e.g. on a GPU box that only runs the prebuilt binaries) this reports False and leaves any
+    binaries already there untouched."""
+    r = subprocess.run(["make", "-C", HERE, "ref"], stdout=subprocess.PIPE,
+                       stderr=subprocess.STDOUT, text=True)
+    if r.returncode != 0:
+        print("note: reference harnesses not rebuilt: " + r.stdout.strip().splitlines()[-1]
+              if r.stdout.strip() else "note: reference harnesses not rebuilt", flush=True)
+    return r.returncode == 0
+
+
 _lib = None
 
 
@@ -98,6 +111,12 @@ def gemm_f64_cols(A, B, cols, C=None, alpha=1.0, beta=0.0, threads=0):
     N = B.shape[1]
     Cb = _halfbits(C) if beta != 0.0 else np.zeros((1, 1), np.uint16)
     cols = np.ascontiguousarray(cols, np.int32)
+    if len(cols) >= 64:
+        # Many columns: the row kernel on B's (and C's) selected columns gives the same sums
+        # in the same k order, blocked and vectorised.
+        Bs = np.ascontiguousarray(B[:, cols])
+        Cs = np.ascontiguousarray(Cb[:, cols]) if beta != 0.0 else None
+        return gemm_f64(A, Bs, Cs, alpha, beta, threads=threads)
     out = np.empty((M, len(cols)), np.float64)
     lib().oracle_gemm_f64_cols(_p(A, _u16p), _p(B, _u16p), _p(Cb, _u16p), _p(out, _f64p), M, N, K,
                                float(alpha), float(beta), _p(cols, _i32p), len(cols), int(threads))

@@ -123,5 +123,19 @@ def test_peer_barrier_wait_gives_up(cuda, oracle):
     assert ok, worst
 
 
+def test_peer_entry_gate(cuda, oracle):
+    """The fused multi-GPU path stores into a peer's C only after that peer has entered the
+    same step. One GPU, local memory only: with the peer's entry flag already set the peer
+    copy is written and equals C; with a flag nobody sets, the gate's bounded wait gives up,
+    records its site, leaves the peer copy untouched, and the local C is still written."""
+    assert cuda.lib.hgemm_selftest_peer_entry(1, 2_000_000_000) == cuda.HGEMM_OK
+    assert cuda.lib.hgemm_selftest_peer_entry(0, 20_000_000) == cuda.HGEMM_ERR_DEVICE_TIMEOUT
+    assert cuda.device_status(clear=True)[0] == 0
+    A, B, _ = _inputs(oracle, 256, 256, 128, seed=11)
+    out = host(cuda.gemm(dev(A), dev(B)))
+    ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B), 128)
+    assert ok, worst
+
+
 def test_device_status_clean(cuda):
     assert cuda.device_status(clear=False)[0] == 0

@@ -1,7 +1,8 @@
 """GPU parity: the sm_100a GEMM, called through the C ABI, against the CPU oracle.
 
 Bars (north_star): every element within |C - C_ref| <= 1e-2 |C_ref| + 2e-3 sqrt(K) of the
-fp64 reference; integer-valued known-answer tests bit-exact; the reference's own suite
+fp64 reference (the whole matrix for every BASELINE config up to 2^40 multiply-adds, sampled
+rows and columns beyond); integer-valued known-answer tests bit-exact; the reference's own suite
 criteria alongside (rel_l2 < 5e-3 vs fp64, check_fp64.cu:46-47; rel_l2 < 3e-3 vs cuBLAS,
 check_all.cu:72); repeated runs bit-identical.
 """
@@ -106,20 +107,29 @@ def test_check_fp64_suite(cuda, oracle, golden_dir):
 @pytest.mark.parametrize("M,N,K", [(4095, 4095, 4095), (4096, 4095, 4096), (2048, 2047, 2048),
                                    (3000, 1000, 2000)])
 def test_ragged_config(cuda, oracle, M, N, K):
-    """alpha=1.5, beta=0.5, C prefilled N(0,1), A/B U[-1,1] (seeded)."""
+    """BASELINE configs[1]: alpha=1.5, beta=0.5, C prefilled N(0,1), A/B U[-1,1] (seeded);
+    every element against the fp64 oracle."""
     g = oracle.MT19937Stream(2024 + M + N + K)
     A = g.uniform_half((M, K), -1.0, 1.0)
     B = g.uniform_half((K, N), -1.0, 1.0)
     C = g.normal_half((M, N), 0.0, 1.0)
     out = run(cuda, A, B, C, 1.5, 0.5)
-    rs = np.random.RandomState(M)
-    rows = np.unique(np.concatenate([rs.randint(0, M, 48), [0, M - 1]]))
-    cols = np.unique(np.concatenate([rs.randint(0, N, 48), [0, N - 1]]))
-    assert_close(oracle, out, A, B, C, 1.5, 0.5, rows=rows)
-    assert_close(oracle, out, A, B, C, 1.5, 0.5, cols=cols)
+    assert_close(oracle, out, A, B, C, 1.5, 0.5)
     # bit-stable: a second run over the same inputs gives the same bits
     out2 = run(cuda, A, B, C, 1.5, 0.5)
     assert np.array_equal(out.view(np.uint16), out2.view(np.uint16))
+
+
+@pytest.mark.parametrize("M,N,K", [(4095, 4095, 4095), (4096, 4095, 4096), (2048, 2047, 2048),
+                                   (3000, 1000, 2000)])
+def test_ragged_config_beta0(cuda, oracle, M, N, K):
+    """The ragged shapes at alpha=1, beta=0 (the reference's perf-table convention) with C
+    prefilled with NaN, which beta=0 must never read; every element against fp64."""
+    g = oracle.MT19937Stream(4048 + M + N + K)
+    A = g.uniform_half((M, K), -1.0, 1.0)
+    B = g.uniform_half((K, N), -1.0, 1.0)
+    out = run(cuda, A, B, None, 1.0, 0.0, nan_c=True)
+    assert_close(oracle, out, A, B, None, 1.0, 0.0)
 
 
 def test_config0_1024_full(cuda, oracle):
@@ -136,22 +146,22 @@ def test_config0_1024_full(cuda, oracle):
                                    (16384, 8192, 128), (2048, 2048, 512), (384, 2048, 2048),
                                    (4096, 512, 4096)])
 def test_thin_k_config(cuda, oracle, M, N, K):
-    """thin-K and skinny shapes."""
+    """thin-K and skinny shapes, every element vs fp64."""
     A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device="cuda"), 0x9E3779B9 ^ K)
     B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device="cuda"), 0x85EBCA6B ^ N)
     C = torch.empty((M, N), dtype=torch.float16, device="cuda")
     cuda.launch(A, B, C, M, N, K, 1.0, 0.0)
     out, hA, hB = host(C), host(A), host(B)
-    rs = np.random.RandomState(K)
-    assert_close(oracle, out, hA, hB, None, 1.0, 0.0, rows=rs.randint(0, M, 64))
-    assert_close(oracle, out, hA, hB, None, 1.0, 0.0, cols=rs.randint(0, N, 64))
+    assert_close(oracle, out, hA, hB, None, 1.0, 0.0)
 
 
 @pytest.mark.parametrize("M,N,K", [(8192, 8192, 8192), (16384, 8192, 4096), (8192, 8192, 16384),
                                    (16384, 16384, 16384)])
 def test_large_config(cuda, oracle, M, N, K):
-    """large shapes, full-entropy fill; sampled rows/cols vs fp64 and
-    the whole matrix vs cuBLAS."""
+    """large shapes, full-entropy fill; the whole matrix vs cuBLAS, and
+    every element vs fp64 up to 2^40 multiply-adds (8192^3, 16384x8192x4096,
+    8192x8192x16384); 16384^3 (2^42) checks 4096 sampled rows and 4096 sampled columns vs
+    fp64."""
     A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device="cuda"), 0x9E3779B9)
     B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device="cuda"), 0x85EBCA6B)
     C = torch.empty((M, N), dtype=torch.float16, device="cuda")
@@ -164,9 +174,12 @@ def test_large_config(cuda, oracle, M, N, K):
     assert l2 < 3e-3, l2
     out, hA, hB = host(C), host(A), host(B)
     del R, diff
-    rs = np.random.RandomState(M + K)
-    assert_close(oracle, out, hA, hB, None, 1.0, 0.0, rows=rs.randint(0, M, 24))
-    assert_close(oracle, out, hA, hB, None, 1.0, 0.0, cols=rs.randint(0, N, 24))
+    if M * N * K <= (1 << 40) * 1.01:
+        assert_close(oracle, out, hA, hB, None, 1.0, 0.0)
+    else:
+        rs = np.random.RandomState(M + K)
+        assert_close(oracle, out, hA, hB, None, 1.0, 0.0, rows=rs.choice(M, 4096, replace=False))
+        assert_close(oracle, out, hA, hB, None, 1.0, 0.0, cols=rs.choice(N, 4096, replace=False))
 
 
 # The reference's check_all.cu shape list (57 shapes): criteria rel_l2 < 3e-3 vs cuBLAS

@@ -128,3 +128,69 @@ def test_two_ranks_fused_peer_stores(cuda, M, N):
         p.join(180)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(out) == {0: True, 1: True}
+
+
+def _steps_worker(rank, world, port, M, N, K, steps, slow_rank, out):
+    """Back-to-back fused calls with a different A every step and a reader of the whole C
+    after each call, without any host-side barrier in between: the slow rank's reader sleeps
+    on the GPU first, so a peer that stored its next step's rows early would show up in the
+    slow rank's snapshot of the previous step."""
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    import hopper_gemm_b200 as hg
+    from hopper_gemm_b200.sharded import RowShardedGemm
+    from tests.gpu_util import hash_fill_
+    b, n = hg.shard_rows(M, world, rank)
+    dB = hash_fill_(torch.empty((K, N), dtype=torch.float16, device="cuda"), 0x85EBCA6B)
+    dC = torch.zeros((M, N), dtype=torch.float16, device="cuda")
+    sg = RowShardedGemm(M, N, K, rank, world)
+    assert sg.register_output(dC)
+    dist.barrier()
+    torch.cuda.synchronize()
+    snaps = []
+    for s in range(steps):
+        A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device="cuda"), 0x51ED + s)
+        sg(A[b:b + n], dB, dC)
+        if rank == slow_rank:
+            torch.cuda._sleep(40_000_000)  # a slow reader: ~20 ms on the stream first
+        snaps.append(dC.clone())           # reads the whole C on the same stream
+    torch.cuda.synchronize()
+    st, where = hg.device_status(clear=True)
+    ok = st == 0
+    for s in range(steps):
+        A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device="cuda"), 0x51ED + s)
+        ref = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        hg.launch(A, dB, ref, M, N, K, 1.0, 0.0)
+        torch.cuda.synchronize()
+        ok = ok and bool(torch.equal(snaps[s].view(torch.int16), ref.view(torch.int16)))
+    out[rank] = (ok, st, where)
+    dist.barrier()
+    sg.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+@pytest.mark.parametrize("N,slow_rank", [(1024, 1), (1024, 0), (1000, 1)])
+def test_two_ranks_fused_back_to_back_steps(cuda, N, slow_rank):
+    # N = 1024: the gated peer-store kernel; N = 1000 (N % 8 != 0): local GEMM, entry barrier
+    # kernel, then copies to the peer.
+    world, M, K, steps = 2, 2048, 512, 4
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_steps_worker, args=(r, world, port, M, N, K, steps, slow_rank,
+                                                     out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(out) == {0: (True, 0, 0), 1: (True, 0, 0)}, dict(out)
