@@ -101,7 +101,10 @@ struct TileCfg {
   // buffer, so 8 warps cost 32 KB of pipeline stages; the planner uses them where the
   // epilogue, not the main loop, sets the pace (see choose_epi_warps).
   static constexpr int EPI_WARPS = EPIW;
-  static constexpr int EPI_BUFS = 2;
+  // The one-accumulator tile (BN = 512) with 8 warps single-buffers its staging, so that it
+  // keeps the 4-warp flavour's pipeline depth: its stores have a whole main loop to drain,
+  // only the TMEM drain between tiles is on the critical path.
+  static constexpr int EPI_BUFS = (ACC_BUFS == 1 && EPIW == 8) ? 1 : 2;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int EPI_COLS_PER_WARP = BN * 4 / EPI_WARPS;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * EPI_ROWS * 128;
@@ -298,6 +301,12 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
   const int first_tile =
       clustered ? static_cast<int>(ptx::cluster_id_x()) : static_cast<int>(blockIdx.x);
 
+  // One accumulator, 8 epilogue warps, TMA stores, beta == 0: warp group g (ew / 4) drains
+  // columns [128 g, 128 g + 128) of each N half, so each half drains twice as fast as with one
+  // group of 4 warps per half (the tensor core has only the deferred slice-1 work of the last
+  // stages to do meanwhile).
+  const bool wide_drain = ACC_BUFS == 1 && Cfg::EPI_WARPS == 8 && TMA_EPI && !SPLITK &&
+                          p.beta == 0.0f;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
@@ -307,7 +316,10 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
       ptx::mbar_init(ptx::smem_u32(&tfull[a]), 1);
       // One accumulator (BN = 512): each N half is drained by 4 warps per CTA (all 4 warps
       // drain both halves, or with 8 warps each group of 4 drains one half).
-      ptx::mbar_init(ptx::smem_u32(&tempty[a]), (ACC_BUFS == 1 ? 4 : Cfg::EPI_WARPS) * PAIR);
+      // With 8 warps and beta == 0 every warp drains a quarter of each half instead
+      // (wide_drain below), so all 8 arrive on both halves.
+      ptx::mbar_init(ptx::smem_u32(&tempty[a]),
+                     (ACC_BUFS == 1 ? (wide_drain ? 8 : 4) : Cfg::EPI_WARPS) * PAIR);
     }
     ptx::mbar_init(ptx::smem_u32(drain), 1);
     // Readers of each tile index: leader MMA + the epilogue warps (+ the peer's producer and
@@ -967,6 +979,68 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
         ++it;
         continue;
       }
+      if constexpr (ACC_BUFS == 1 && TMA_EPI && Cfg::EPI_WARPS == 8 && !SPLITK) {
+        if (wide_drain) {
+          // Each half: two batches of 64 TMEM columns into packed halves, the half handed
+          // back right after the second wait, then two 32 x 64 chunks through this warp's
+          // single staging buffer.
+          const int g = ew >> 2;
+          bool aborted = false;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !wait_half1()) {
+              aborted = true;
+              break;
+            }
+            const uint32_t ta = tbase + static_cast<uint32_t>(h * (BN / 2) + g * 128);
+            uint32_t P[64];
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              uint32_t v[64];
+              ptx::tmem_ld_32x32b_x32(ta + 64 * b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+              ptx::tmem_ld_32x32b_x32(ta + 64 * b + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+              ptx::tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                P[32 * b + i] = pack_half2(alpha * __uint_as_float(v[2 * i]),
+                                           alpha * __uint_as_float(v[2 * i + 1]));
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              const uint32_t tb = tempty_leader + static_cast<uint32_t>(h) * 8u;
+              if (PAIR == 2)
+                ptx::mbar_arrive_remote(tb);
+              else
+                ptx::mbar_arrive(tb);
+            }
+            const uint32_t stg_base = ptx::smem_u32(stg0) + static_cast<uint32_t>(lane) * 128u;
+            const uint32_t sw = static_cast<uint32_t>(lane & 7);
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch, ++chunk_ctr) {
+              // The TMA store of the previous chunk must have read the staging buffer.
+              if (lane == 0) ptx::bulk_wait_group_read<0>();
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                ptx::st_shared_v4(stg_base + ((static_cast<uint32_t>(j) ^ sw) << 4),
+                                  P[32 * ch + 4 * j + 0], P[32 * ch + 4 * j + 1],
+                                  P[32 * ch + 4 * j + 2], P[32 * ch + 4 * j + 3]);
+              ptx::fence_proxy_async_smem();
+              __syncwarp();
+              const int ccol = col0 + h * (BN / 2) + g * 128 + ch * EPI_COLS;
+              if (lane == 0) {
+                if (row0 < p.M && ccol < p.N) store_c(&tmC, ptx::smem_u32(stg0), ccol, row0);
+                ptx::bulk_commit_group();
+              }
+              if (npeer_live > 0) push_peers(stg0, row0, ccol);
+            }
+          }
+          if (aborted) break;
+          ++it;
+          continue;
+        }
+      }
       if constexpr (ACC_BUFS == 1 && TMA_EPI && Cfg::EPI_WARPS == 4) {
         if (beta == 0.0f) {
           // Single accumulator: drain each N half into registers as packed halves, give that
@@ -1585,8 +1659,13 @@ int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b
 // pace, tiles of at most 2 k-blocks (K <= 128: 4096x8192x128 0.78 -> 0.91 of cuBLAS,
 // 16384x8192x128 0.89 -> 1.00 on B200); from K = 256 the 32 KB of pipeline stages they cost
 // weigh more (4096x8192x256 on 256x256: 0.85 with 4 warps, 0.80 with 8).
-int choose_epi_warps(int tile, int kbn) {
+// The one-accumulator 256x512 tile with beta == 0 takes 8 warps that each drain a quarter of
+// every N half (wide_drain in the kernel), which shortens the hand-off between its tiles
+// (B200, paired with cuBLAS, three runs each: 8192x8192x4096 0.961 -> 0.970,
+// 16384x8192x4096 0.972 -> 0.979, 8192^3 0.982 -> 0.984).
+int choose_epi_warps(int tile, int kbn, float beta) {
   if (tile == kT128x64) return 4;
+  if (tile == kT256x512) return beta == 0.0f ? 8 : 4;
   return kbn <= 2 ? 8 : 4;
 }
 
@@ -1697,7 +1776,7 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   {
     const int kbn0 = ceil_div(K, BK);
     const int flav = !pl->tma_store ? kFlavSimt
-                     : (choose_epi_warps(tile, kbn0) == 8 ? kFlavE8 : kFlavE4);
+                     : (choose_epi_warps(tile, kbn0, beta) == 8 ? kFlavE8 : kFlavE4);
     pl->stages = ti.flav[flav].stages;
     pl->epi_warps = ti.flav[flav].epi_warps;
   }

@@ -50,7 +50,8 @@ def test_reference_check_all(cuda):
     rc, out, err = _run("check_all")
     rows = _rows(out)
     assert len(rows) == 57, out[-2000:] + err[-2000:]
-    bad = [r for r in rows if not r[7].strip().startswith("OK")]
+    # each row ends with its source tag and the harness's verdict ("OK" or "*** FAIL ***")
+    bad = [r for r in rows if r[7].split()[-1] != "OK" or "FAIL" in r[7]]
     assert not bad, bad
     assert "57 shapes, 0 failures" in out
     assert rc == 0
@@ -60,7 +61,8 @@ def test_reference_check_large(cuda):
     rc, out, err = _run("check_large")
     rows = _rows(out)
     assert len(rows) == 12, out[-2000:] + err[-2000:]
-    bad = [r for r in rows if not r[7].strip().startswith("OK")]
+    # each row's verdict ("OK" or "*** FAIL ***") comes before the row's note
+    bad = [r for r in rows if r[7].split()[0] != "OK" or "FAIL" in r[7]]
     assert not bad, bad
     assert rc == 0
 
