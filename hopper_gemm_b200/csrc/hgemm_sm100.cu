@@ -1379,35 +1379,115 @@ __global__ void __launch_bounds__(256) hgemm_simt_kernel(const __half *__restric
   }
 }
 
-// Copy a rows x cols half matrix into a buffer with a 16-byte-aligned row stride `ld`
-// (ld % 8 == 0); the pad columns are written as zeros. One 16-byte store per thread step.
-__global__ void __launch_bounds__(256) restride_kernel(const __half *__restrict__ src,
-                                                       __half *__restrict__ dst, int rows,
-                                                       int cols, int ld) {
-  const long long groups_per_row = ld / 8;
-  const long long total = static_cast<long long>(rows) * groups_per_row;
-  for (long long g = blockIdx.x * 256LL + threadIdx.x; g < total; g += 256LL * gridDim.x) {
-    const int r = static_cast<int>(g / groups_per_row);
-    const int c = static_cast<int>(g - r * groups_per_row) * 8;
-    const __half *s = src + static_cast<long long>(r) * cols;
-    __align__(16) __half v[8];
+// ---------------------------------------------------------------- restride / compact
+// HBM-bound copies between a row-major matrix whose rows are not 16-byte aligned (row length
+// `cols` halves, cols % 8 != 0) and a copy with a 16-byte row stride `ld` (ld % 8 == 0), the
+// layout TMA needs. Every thread moves one 16-byte group of 8 halves with one 16-byte store;
+// the 8 source halves, which start at an arbitrary even byte offset, come from the (at most
+// two) aligned 16-byte blocks that contain the first and the last of them, merged with funnel
+// shifts. Both blocks contain an element that is read, so no load reaches past the matrix.
+
+// 16 bytes starting `shift` bytes (even, < 16) into the 32 bytes lo:hi. The shift depends on
+// the row only (group starts are 16 bytes apart), so it is uniform across most warps.
+__device__ __forceinline__ uint4 extract16(const uint4 lo, const uint4 hi, uint32_t shift) {
+  const uint32_t b = (shift & 3u) * 8u;
+  switch (shift >> 2) {
+    case 0: return make_uint4(__funnelshift_r(lo.x, lo.y, b), __funnelshift_r(lo.y, lo.z, b),
+                              __funnelshift_r(lo.z, lo.w, b), __funnelshift_r(lo.w, hi.x, b));
+    case 1: return make_uint4(__funnelshift_r(lo.y, lo.z, b), __funnelshift_r(lo.z, lo.w, b),
+                              __funnelshift_r(lo.w, hi.x, b), __funnelshift_r(hi.x, hi.y, b));
+    case 2: return make_uint4(__funnelshift_r(lo.z, lo.w, b), __funnelshift_r(lo.w, hi.x, b),
+                              __funnelshift_r(hi.x, hi.y, b), __funnelshift_r(hi.y, hi.z, b));
+    default: return make_uint4(__funnelshift_r(lo.w, hi.x, b), __funnelshift_r(hi.x, hi.y, b),
+                               __funnelshift_r(hi.y, hi.z, b), __funnelshift_r(hi.z, hi.w, b));
+  }
+}
+
+// `n` (1..8) consecutive halves starting at p, in the low lanes of a 16-byte group; the rest
+// of the group is zero.
+__device__ __forceinline__ uint4 load_halves(const __half *p, int n) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(p);
+  const uintptr_t a1 = a0 + 2u * static_cast<uintptr_t>(n - 1);
+  const uint4 lo = __ldg(reinterpret_cast<const uint4 *>(a0 & ~uintptr_t(15)));
+  const uint4 hi = ((a1 & ~uintptr_t(15)) != (a0 & ~uintptr_t(15)))
+                       ? __ldg(reinterpret_cast<const uint4 *>(a1 & ~uintptr_t(15)))
+                       : lo;
+  uint4 v = extract16(lo, hi, static_cast<uint32_t>(a0 & 15u));
+  if (n < 8) {
+    uint32_t *vw = reinterpret_cast<uint32_t *>(&v);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = (c + e < cols) ? s[c + e] : __float2half(0.0f);
-    *reinterpret_cast<uint4 *>(dst + static_cast<long long>(r) * ld + c) =
-        *reinterpret_cast<const uint4 *>(v);
+    for (int j = 0; j < 4; ++j) {
+      const int e = 2 * j;  // halves e, e + 1 live in word j
+      if (e >= n) vw[j] = 0u;
+      else if (e + 1 >= n) vw[j] &= 0xffffu;
+    }
+  }
+  return v;
+}
+
+// Up to three restrides in one launch (A, B and C of one GEMM): job j covers groups
+// [first[j], first[j + 1]) of the grid-stride range.
+struct RestrideJobs {
+  const __half *src[3];
+  __half *dst[3];
+  int rows[3], cols[3], ld[3];
+  long long first[4];
+  long long total;  // first[n]
+  int n;
+};
+__global__ void __launch_bounds__(256) restride_kernel(const RestrideJobs jb) {
+  const long long total = jb.total;
+  for (long long g = blockIdx.x * 256LL + threadIdx.x; g < total; g += 256LL * gridDim.x) {
+    // The job's fields, selected with constant indices (an array of kernel parameters
+    // indexed at run time would be copied to local memory).
+    const __half *src = jb.src[0];
+    __half *dst = jb.dst[0];
+    int cols = jb.cols[0], ld = jb.ld[0];
+    long long first = 0;
+#pragma unroll
+    for (int j = 1; j < 3; ++j) {
+      if (j < jb.n && g >= jb.first[j]) {
+        src = jb.src[j];
+        dst = jb.dst[j];
+        cols = jb.cols[j];
+        ld = jb.ld[j];
+        first = jb.first[j];
+      }
+    }
+    const long long gj = g - first;
+    const int gpr = ld / 8;
+    const int r = static_cast<int>(gj / gpr);
+    const int c = static_cast<int>(gj - static_cast<long long>(r) * gpr) * 8;
+    const int n = min(8, cols - c);
+    const uint4 v = n > 0 ? load_halves(src + static_cast<long long>(r) * cols + c, n)
+                          : make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4 *>(dst + static_cast<long long>(r) * ld + c) = v;
   }
 }
 
 // Inverse of restride_kernel: rows x cols out of a buffer with row stride `ld` into a
-// row-major rows x cols matrix. One element per thread step; consecutive lanes take
-// consecutive columns, so loads and stores are coalesced.
+// row-major rows x cols matrix `dst` (16-byte aligned). Thread t writes elements
+// [8t, 8t + 8) of dst with one 16-byte store; groups that cross a row end, and the last
+// partial group, take their halves one by one.
 __global__ void __launch_bounds__(256) compact_kernel(const __half *__restrict__ src,
                                                       __half *__restrict__ dst, int rows,
                                                       int cols, int ld) {
   const long long total = static_cast<long long>(rows) * cols;
-  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += 256LL * gridDim.x) {
-    const long long r = i / cols;
-    dst[i] = src[r * ld + (i - r * cols)];
+  const long long groups = (total + 7) / 8;
+  for (long long t = blockIdx.x * 256LL + threadIdx.x; t < groups; t += 256LL * gridDim.x) {
+    const long long o = 8 * t;
+    const long long r = o / cols;
+    const int c = static_cast<int>(o - r * cols);
+    if (c + 8 <= cols && o + 8 <= total) {
+      *reinterpret_cast<uint4 *>(dst + o) = load_halves(src + r * ld + c, 8);
+    } else {
+      const int n = static_cast<int>(min(8LL, total - o));
+      for (int e = 0; e < n; ++e) {
+        const long long oe = o + e;
+        const long long re = oe / cols;
+        dst[oe] = src[re * ld + (oe - re * cols)];
+      }
+    }
   }
 }
 
@@ -1869,12 +1949,24 @@ void *scratch_get(DevState &d, size_t bytes) {
   return p;
 }
 
-int launch_restride(const __half *src, __half *dst, int rows, int cols, int ld, int sm_count,
-                    cudaStream_t stream) {
-  const long long groups = static_cast<long long>(rows) * (ld / 8);
+// One launch for every operand of a GEMM that needs a 16-byte row stride.
+int launch_restrides(const RestrideJobs &jobs, int sm_count, cudaStream_t stream) {
+  if (jobs.n == 0) return HGEMM_OK;
+  const long long groups = jobs.total;
   const int blocks = static_cast<int>(std::min<long long>((groups + 255) / 256, sm_count * 8LL));
-  restride_kernel<<<std::max(blocks, 1), 256, 0, stream>>>(src, dst, rows, cols, ld);
+  restride_kernel<<<std::max(blocks, 1), 256, 0, stream>>>(jobs);
   return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
+}
+
+void add_restride(RestrideJobs &jobs, const __half *src, __half *dst, int rows, int cols, int ld) {
+  const int j = jobs.n++;
+  jobs.src[j] = src;
+  jobs.dst[j] = dst;
+  jobs.rows[j] = rows;
+  jobs.cols[j] = cols;
+  jobs.ld[j] = ld;
+  jobs.first[j + 1] = jobs.first[j] + static_cast<long long>(rows) * (ld / 8);
+  jobs.total = jobs.first[j + 1];
 }
 
 int launch_simt(const __half *A, const __half *B, __half *C, int M, int N, int K, float alpha,
@@ -1980,8 +2072,8 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
 
 int launch_compact(const __half *src, __half *dst, int rows, int cols, int ld, int sm_count,
                    cudaStream_t stream) {
-  const long long n = static_cast<long long>(rows) * cols;
-  const int blocks = static_cast<int>(std::min<long long>((n + 255) / 256, sm_count * 8LL));
+  const long long groups = (static_cast<long long>(rows) * cols + 7) / 8;
+  const int blocks = static_cast<int>(std::min<long long>((groups + 255) / 256, sm_count * 8LL));
   compact_kernel<<<std::max(blocks, 1), 256, 0, stream>>>(src, dst, rows, cols, ld);
   return cudaGetLastError() == cudaSuccess ? HGEMM_OK : HGEMM_ERR_LAUNCH;
 }
@@ -1999,23 +2091,22 @@ int launch_padded(const hgemm_plan_t &pl, const __half *A, const __half *B, __ha
   __half *Cuse = C;
   const size_t na = pl.pad_a ? static_cast<size_t>(M) * pl.lda : 0;
   const size_t nb = pl.pad_b ? static_cast<size_t>(K) * pl.ldb : 0;
+  RestrideJobs jobs;
+  std::memset(&jobs, 0, sizeof(jobs));
   if (pl.pad_a) {
-    st = launch_restride(A, w, M, K, pl.lda, d.sm_count, stream);
-    if (st != HGEMM_OK) return st;
+    add_restride(jobs, A, w, M, K, pl.lda);
     Ause = w;
   }
   if (pl.pad_b) {
-    st = launch_restride(B, w + na, K, N, pl.ldb, d.sm_count, stream);
-    if (st != HGEMM_OK) return st;
+    add_restride(jobs, B, w + na, K, N, pl.ldb);
     Buse = w + na;
   }
   if (pl.pad_c) {
     Cuse = w + na + nb;
-    if (beta != 0.0f) {
-      st = launch_restride(C, Cuse, M, N, pl.ldc, d.sm_count, stream);
-      if (st != HGEMM_OK) return st;
-    }
+    if (beta != 0.0f) add_restride(jobs, C, Cuse, M, N, pl.ldc);
   }
+  st = launch_restrides(jobs, d.sm_count, stream);
+  if (st != HGEMM_OK) return st;
   int tile = -1;
   for (int t = 0; t < kNumTiles; ++t)
     if (kTiles[t].pair == pl.pair && kTiles[t].bn == pl.tile_n) tile = t;

@@ -241,3 +241,19 @@ def test_every_tile(cuda, oracle, tile, M, N, K, al, be):
     C = g.normal_half((M, N)) if be != 0 else None
     out = run(cuda, A, B, C, al, be, via="launch", force=tile, nan_c=(be == 0))
     assert_close(oracle, out, A, B, C, al, be)
+
+
+# ---------------------------------------------------------------- restride / compact edges
+@pytest.mark.parametrize("K", [1, 3, 7, 9, 15, 17, 63, 65, 129])
+def test_ragged_restride_edges(cuda, oracle, K):
+    """K % 8 != 0 (A restrided) against N in {1, 3, 5, 9, 17, 31, 33, 127, 129} (B restrided
+    and, with beta != 0, C copied to a 16-byte row stride and back): every element vs fp64,
+    for the fused 16-byte restride copies and the compaction of C."""
+    g = oracle.MT19937Stream(9000 + K)
+    for N in (1, 3, 5, 9, 17, 31, 33, 127, 129):
+        for M, al, be in ((37, 1.0, 0.0), (130, -0.75, 1.25)):
+            A = g.uniform_half((M, K))
+            B = g.uniform_half((K, N))
+            C = g.normal_half((M, N))
+            out = run(cuda, A, B, C if be != 0 else None, al, be, nan_c=(be == 0))
+            assert_close(oracle, out, A, B, C if be != 0 else None, al, be)
