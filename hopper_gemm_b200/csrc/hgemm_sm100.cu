@@ -134,6 +134,7 @@ struct KParams {
   int ldc;            // row stride of C in halves (N, or N rounded up to 8 for the padded copy)
   int ksplit;         // > 1 (one-CTA tiles only): a cluster of ksplit CTAs shares each tile's
                       // k-blocks and reduces the partial sums over distributed shared memory
+  int b4;             // 1: tmB is the 4-D view of B (every tile whole in N): one load per stage
 };
 
 // Other destinations of every C tile (e.g. the C buffers of peer GPUs mapped into this
@@ -417,16 +418,25 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
             ptx::tma_load_2d_pair(&tmA, dA, fbar, kb * BK, arow);
           else
             ptx::tma_load_2d(&tmA, dA, fbar, kb * BK, arow);
+          if (p.b4) {
+            // All N_SUB x SUB_BOXES blocks of 64 columns in one instruction: coordinates are
+            // (column in block, k, first 64-column block of this CTA's slice 0, slice).
+            if (PAIR == 2)
+              ptx::tma_load_4d_pair(&tmB, dB, fbar, 0, kb * BK, bcol / 64, 0);
+            else
+              ptx::tma_load_4d(&tmB, dB, fbar, 0, kb * BK, bcol / 64, 0);
+          } else {
 #pragma unroll
-          for (int j = 0; j < Cfg::N_SUB; ++j) {
+            for (int j = 0; j < Cfg::N_SUB; ++j) {
 #pragma unroll
-            for (int b = 0; b < Cfg::SUB_BOXES; ++b) {
-              const uint32_t dst = dB + static_cast<uint32_t>(j * Cfg::SUB_BOXES + b) * (BK * 128);
-              const int col = bcol + j * Cfg::UMMA_N + 64 * b;
-              if (PAIR == 2)
-                ptx::tma_load_2d_pair(&tmB, dst, fbar, col, kb * BK);
-              else
-                ptx::tma_load_2d(&tmB, dst, fbar, col, kb * BK);
+              for (int b = 0; b < Cfg::SUB_BOXES; ++b) {
+                const uint32_t dst = dB + static_cast<uint32_t>(j * Cfg::SUB_BOXES + b) * (BK * 128);
+                const int col = bcol + j * Cfg::UMMA_N + 64 * b;
+                if (PAIR == 2)
+                  ptx::tma_load_2d_pair(&tmB, dst, fbar, col, kb * BK);
+                else
+                  ptx::tma_load_2d(&tmB, dst, fbar, col, kb * BK);
+              }
             }
           }
           ++issued;
@@ -1588,6 +1598,28 @@ bool encode_2d(CUtensorMap *map, const void *ptr, int rows, int cols, long long 
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// B (K x N row-major, row stride ld halves) as a 4-D tensor for the producer's one-instruction
+// stage load: dimensions (64 columns of a block, K, 64-column blocks of one UMMA slice, slices)
+// with strides (2 bytes, ld * 2, 128 bytes, umma_n * 2 bytes). Dimensions 2 and 3 alias: block
+// c2 of slice c3 is column block c2 + c3 * umma_n / 64, which the map cannot bounds-check, so
+// it is only used when every tile is whole in N (N % tile_n == 0). The box of
+// 64 x 64 x boxes x slices lands as consecutive 8 KB blocks, the layout of the 2-D loads.
+bool encode_b4(CUtensorMap *map, const void *ptr, int K, int N, long long ld, int umma_n,
+               int boxes, int slices) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[4] = {64, static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N / 64),
+                        static_cast<cuuint64_t>(N / umma_n)};
+  cuuint64_t gstride[3] = {static_cast<cuuint64_t>(ld) * sizeof(__half), 128,
+                           static_cast<cuuint64_t>(umma_n) * sizeof(__half)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(boxes),
+                       static_cast<cuuint32_t>(slices)};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), gdim, gstride, box,
+             estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ---------------------------------------------------------------- kernel table
 enum TileId {
   kT256x512 = 0,
@@ -1992,7 +2024,12 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   const TileInfo &ti = kTiles[tile];
   const bool tma_epi = pl.tma_store != 0;
   CUtensorMap ta, tb, tc;
-  if (!encode_2d(&ta, A, M, K, lda, CTA_M, BK) || !encode_2d(&tb, B, K, N, ldb, BK, 64))
+  const int umma_n = ti.bn < 256 ? ti.bn : 256;
+  const int sub_boxes = umma_n / ti.pair / 64, n_sub = ti.bn / umma_n;
+  // One 4-D load per stage for B when every tile is whole in N (see encode_b4).
+  const bool b4 = (N % ti.bn == 0) && sub_boxes * n_sub > 1 &&
+                  encode_b4(&tb, B, K, N, ldb, umma_n, sub_boxes, n_sub);
+  if (!encode_2d(&ta, A, M, K, lda, CTA_M, BK) || (!b4 && !encode_2d(&tb, B, K, N, ldb, BK, 64)))
     return HGEMM_ERR_TENSOR_MAP;
   if (tma_epi) {
     if (!encode_2d(&tc, C, M, N, pl.ldc, EPI_ROWS, EPI_COLS)) return HGEMM_ERR_TENSOR_MAP;
@@ -2019,8 +2056,8 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   }
   const int flav = !tma_epi ? kFlavSimt
                    : pl.ksplit > 1 ? kFlavSplit
-                   : npeers > 0 ? (pl.epi_warps == 8 ? kFlavPeerE8 : kFlavPeerE4)
-                   : (pl.epi_warps == 8 ? kFlavE8 : kFlavE4);
+                   : npeers > 0 ? (pl.epi_warps >= 8 ? kFlavPeerE8 : kFlavPeerE4)
+                   : (pl.epi_warps >= 8 ? kFlavE8 : kFlavE4);
   const FlavorInfo &fi = ti.flav[flav];
   KernelFn k = kernel_for(tile, flav);
   if (!k) return npeers > 0 ? HGEMM_ERR_NOT_FUSABLE : HGEMM_ERR_INVALID_ARG;
@@ -2048,6 +2085,7 @@ int launch_tc(const hgemm_plan_t &pl, int tile, const __half *A, int lda, const 
   kp.timeout_ns = g_timeout_ns.load();
   kp.sched_static = pl.sched_static;
   kp.ksplit = pl.ksplit > 1 ? pl.ksplit : 1;
+  kp.b4 = b4 ? 1 : 0;
   // Peer copies are never read on the receiving GPU during the step either.
   kp.c_evict_first = (K >= kCEvictFirstMinK || npeers > 0) ? 1 : 0;
 

@@ -200,6 +200,25 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap *m, uint32_t 
       "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1)
       : "memory");
 }
+// 4-D tiled loads: one instruction for a box of several 64-column blocks of B (see the B
+// tensor map in launch_tc). Same completion and pair semantics as the 2-D forms above.
+__device__ __forceinline__ void tma_load_4d(const CUtensorMap *m, uint32_t dst, uint32_t bar,
+                                            int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_pair(const CUtensorMap *m, uint32_t dst,
+                                                 uint32_t bar_cluster, int32_t c0, int32_t c1,
+                                                 int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 // L2 policy that marks lines as the first to evict (streamed output that no CTA re-reads).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;
