@@ -88,6 +88,9 @@ def parse():
     ap.add_argument("--config5-steps", type=int, default=10)
     ap.add_argument("--grid-child", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--grid-index", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--peer-standins", type=int, default=0,
+                    help="with --grid: run the peer-store flavour of the fused multi-GPU path with "
+                         "this many same-GPU buffers standing in for the peers' C (0-7)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -122,7 +125,7 @@ def profiled_traffic(M, N, K):
 
 
 class ClockSampler:
-    """SM clock, power and throttle reasons sampled through NVML every 10 ms while the timed
+    """SM clock, power and throttle reasons sampled through NVML every 2 ms while the timed
     region runs (falls back to `nvidia-smi -lms 100` when pynvml is missing)."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
@@ -146,7 +149,7 @@ class ClockSampler:
                                      pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
             except pynvml.NVMLError:
                 pass
-            self.stop.wait(0.01)
+            self.stop.wait(0.002)
 
     def _poll_smi(self):
         fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
@@ -293,6 +296,7 @@ GRID_RAGGED = [(4095, 4095, 4095), (4096, 4095, 4096), (2048, 2047, 2048), (3000
 
 
 def run_grid(args):
+    import ctypes
     """Reference methodology per shape (three_way.cu): hash-filled A/B, 5 interleaved
     warm-ups, then `reps` rounds of {3x L2 memset, event, one launch, event} for ours, for
     cuBLAS and (16-byte aligned shapes, when it was built) for the CUTLASS SM100 comparator;
@@ -325,7 +329,8 @@ def run_grid(args):
             spec = f"{M}x{N}x{K}:{al}/{be}"
             subprocess.run([sys.executable, os.path.abspath(__file__), "--grid", "--grid-child",
                             "--grid-shapes", spec, "--grid-index", str(i),
-                            "--grid-reps", str(args.grid_reps)], check=True)
+                            "--grid-reps", str(args.grid_reps),
+                            "--peer-standins", str(args.peer_standins)], check=True)
         return
     for i, (M, N, K, al, be) in enumerate(cases, start=args.grid_index):
         A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device=dev), 0x9E3779B9 ^ i)
@@ -334,10 +339,21 @@ def run_grid(args):
         R = C.clone()
         C0 = C.clone()
         T = C.clone()
-        use_cut = cut is not None and N % 8 == 0 and K % 8 == 0
+        use_cut = cut is not None and N % 8 == 0 and K % 8 == 0 and K > 0
+        # --peer-standins P: ours runs the fused multi-GPU path's peer-store kernel flavour
+        # with P same-GPU buffers standing in for the peers' C (the SM-side cost of the peer
+        # copies on one GPU, and a one-GPU target for profiling that kernel)
+        stand = [torch.empty((M, N), dtype=torch.float16, device=dev)
+                 for _ in range(args.peer_standins)]
+        stand_arr = (ctypes.c_void_p * max(1, len(stand)))(*[t.data_ptr() for t in stand])
 
         def ours():
-            st = hg.lib.hgemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, al, be, sptr)
+            if stand:
+                st = hg.lib.hgemm_launch_peers(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K,
+                                               al, be, sptr, stand_arr, len(stand), 0)
+            else:
+                st = hg.lib.hgemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, al,
+                                         be, sptr)
             if st != 0:
                 raise RuntimeError(hg.status_string(st))
 
@@ -395,9 +411,9 @@ def run_grid(args):
             "paired_ratio_vs_cutlass": (statistics.median(t / o for o, t in zip(to, tt))
                                         if tt else None),
             "rel_l2_vs_cublas": l2, "rel_l2_vs_cutlass": l2t,
-            "tile": f"{plan['tile_m']}x{plan['tile_n']}",
+            "tile": f"{plan['tile_m']}x{plan['tile_n']}", "peer_standins": len(stand),
             "restride": bool(plan["pad_a"] or plan["pad_b"])}), flush=True)
-        del A, B, C, R, C0, T
+        del A, B, C, R, C0, T, stand
         torch.cuda.empty_cache()
 
 
