@@ -68,3 +68,24 @@ def test_noalloc_rejects_oversize_without_work(cuda):
     assert plan["scratch_bytes"] > lib.hgemm_noalloc_scratch_bytes()
     assert st == cuda._native.HGEMM_ERR_TOO_LARGE
     assert bool((C == 7.0).all())  # nothing ran
+
+
+def test_noalloc_padded_c_counts_against_the_array(cuda):
+    """The padded C copy (N % 8 != 0 with beta != 0) also comes from the fixed array: here it
+    alone is over the limit (A needs no restride, B is 8 rows), so the same shape runs with
+    beta == 0 and is rejected, untouched, with beta != 0."""
+    lib = cuda.lib
+    M, N, K = 8192, 8191, 8
+    cap = lib.hgemm_noalloc_scratch_bytes()
+    p0, p1 = cuda.plan(M, N, K, beta=0.0), cuda.plan(M, N, K, beta=0.5)
+    assert not p1["pad_a"] and p1["pad_c"] and p1["scratch_bytes"] > cap
+    assert not p0["pad_c"] and p0["scratch_bytes"] <= cap
+    A = torch.ones((M, K), dtype=torch.float16, device="cuda")
+    B = torch.ones((K, N), dtype=torch.float16, device="cuda")
+    C = torch.full((M, N), 7.0, dtype=torch.float16, device="cuda")
+    assert _call(lib.hgemm_launch_noalloc, A, B, C, M, N, K, 1.0, 0.5) == \
+        cuda._native.HGEMM_ERR_TOO_LARGE
+    assert bool((C == 7.0).all())  # nothing ran
+    assert _call(lib.hgemm_launch_noalloc, A, B, C, M, N, K, 1.0, 0.0) == 0
+    assert bool((C == float(K)).all())
+    assert cuda.device_status(clear=True)[0] == 0
