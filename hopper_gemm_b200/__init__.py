@@ -18,7 +18,8 @@ from . import _native
 from ._native import (HGEMM_ERR_DEVICE_TIMEOUT, HGEMM_ERR_INVALID_ARG, HGEMM_OK,  # noqa: F401
                       HgemmPlan, lib)
 
-__all__ = ["solve", "launch", "launch_tuned", "gemm", "plan", "last_status", "status_string",
+__all__ = ["solve", "launch", "launch_tuned", "launch_host", "gemm", "plan", "last_status",
+           "status_string",
            "device_status", "release", "HgemmError", "set_wait_timeout_ns",
            "selftest_wait_timeout", "shard_rows"]
 
@@ -74,6 +75,17 @@ def launch_tuned(A, B, C, M, N, K, alpha=1.0, beta=0.0, stream=None):
                                 float(alpha), float(beta), _stream(stream))
     if st != HGEMM_OK:
         raise HgemmError(st, "hgemm_launch_tuned")
+
+
+def launch_host(A_h, B_h, C_h, dA, dB, dC, M, N, K, alpha=1.0, beta=0.0, stream=None):
+    """GEMM on host buffers (page-locked for overlap) through caller-owned device buffers:
+    the copies in and out run in row blocks overlapped with the GEMM (hgemm_launch_host).
+    Asynchronous: C_h holds the result once `stream` has passed the call."""
+    st = lib.hgemm_launch_host(_addr(A_h), _addr(B_h), _addr(C_h), _addr(dA), _addr(dB),
+                               _addr(dC), int(M), int(N), int(K), float(alpha), float(beta),
+                               _stream(stream))
+    if st != HGEMM_OK:
+        raise HgemmError(st, "hgemm_launch_host")
 
 
 def gemm(A, B, C=None, alpha=1.0, beta=0.0, stream=None):

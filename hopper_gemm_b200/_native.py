@@ -53,6 +53,7 @@ SIGNATURES = {
     "hgemm_launch_peers": (_i, _GEMM + [_vp, _vp, _i, _i]),
     "hgemm_launch_noalloc": (_i, _GEMM + [_vp]),
     "hgemm_noalloc_scratch_bytes": (ctypes.c_size_t, []),
+    "hgemm_launch_host": (_i, [_vp] * 6 + [_i, _i, _i, _f, _f, _vp]),
     "hgemm_last_status": (_i, []),
     "hgemm_status_string": (ctypes.c_char_p, [_i]),
     "hgemm_device_status": (_i, [_i, ctypes.POINTER(_i)]),

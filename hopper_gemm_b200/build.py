@@ -1,7 +1,8 @@
 """Build recipe for the in-tree CUDA libraries (sm_100a only).
 
 Produces, next to this file:
-  libhgemm_b200.so       the GEMM product: tcgen05 kernel, dispatcher, C ABI, NCCL row shards
+  libhgemm_b200.so       the GEMM product: tcgen05 kernel, dispatcher, C ABI, NCCL row shards,
+                         host-buffer pipeline
   libhgemm_cublas_ref.so the cuBLAS comparator used by bench.py and the GPU tests
   libhgemm_cutlass_ref.so the CUTLASS SM100 comparator (third grid column, cross-check tests),
                          built when CUTLASS's headers are found (the copies vendored in the
@@ -67,7 +68,7 @@ def build(force=False, verbose=True, extra_flags=()):
     nvcc = _nvcc()
     common = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE,
                      "-I" + CSRC] + list(extra_flags)
-    srcs = [os.path.join(CSRC, f) for f in ("hgemm_sm100.cu", "hgemm_sharded.cpp")]
+    srcs = [os.path.join(CSRC, f) for f in ("hgemm_sm100.cu", "hgemm_sharded.cpp", "hgemm_host.cpp")]
     deps = srcs + [os.path.join(CSRC, "ptx_sm100.cuh"), os.path.join(INCLUDE, "hgemm_b200.h")]
     if force or _stale(LIB, deps):
         _run([nvcc] + common + ["-shared", "-o", LIB] + srcs + ["-ldl"], verbose)

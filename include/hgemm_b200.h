@@ -96,6 +96,20 @@ int hgemm_launch_noalloc(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_hal
                          int N, int K, float alpha, float beta, hgemm_stream_t stream);
 size_t hgemm_noalloc_scratch_bytes(void);
 
+/* Host-buffer GEMM (no counterpart in the reference, whose solve() takes device pointers):
+ * A_h, B_h and C_h are HOST pointers (page-locked, e.g. from cudaHostAlloc, for the copies to
+ * run asynchronously), dA, dB, dC caller-owned device buffers of the full M x K, K x N and
+ * M x N sizes. The call copies B in, then the rows of A (and of C when beta != 0) in blocks of
+ * whole 256-row multiples; the GEMM of each block runs on `stream` as soon as its rows have
+ * landed, and each finished block of C is copied back to C_h while later blocks are still
+ * being copied in and computed, so the transfers in both directions overlap the math.
+ * Asynchronous: C_h holds the result once `stream` passes the call (the library's own copy
+ * streams are joined back into it). Same semantics and status codes as hgemm_launch; a shape
+ * with N % 8 != 0 runs as one block. Calls on one device are serialised on the host. */
+int hgemm_launch_host(const hgemm_half_t *A_h, const hgemm_half_t *B_h, hgemm_half_t *C_h,
+                      hgemm_half_t *dA, hgemm_half_t *dB, hgemm_half_t *dC, int M, int N, int K,
+                      float alpha, float beta, hgemm_stream_t stream);
+
 /* ---------------------------------------------------------------- status, planning */
 
 /* Status of the last call made by this host thread. */
@@ -241,8 +255,9 @@ int hgemm_comm_set_reserved_sms(hgemm_comm_t comm, int sms);
 
 /* A_local: this rank's rows of A (rows x K); B: full K x N on this device; C: full M x N on
  * this device (the local row block is read when beta != 0). Equal row blocks
- * (M % nranks == 0) gather in place with one ncclAllGather; otherwise per-rank broadcasts.
- * `chunks` > 1 splits the local rows so the gather of chunk c overlaps the GEMM of c+1. */
+ * (M % nranks == 0) gather in place with one ncclAllGather; otherwise grouped
+ * ncclSend/ncclRecv of each rank's rows to every peer. `chunks` > 1 splits the local rows so
+ * the gather of chunk c (grouped sends and receives) overlaps the GEMM of c+1. */
 int hgemm_sharded_rank(hgemm_comm_t comm, const hgemm_half_t *A_local, const hgemm_half_t *B,
                        hgemm_half_t *C, int M, int N, int K, float alpha, float beta,
                        int chunks, hgemm_stream_t stream);

@@ -52,6 +52,13 @@ def test_invalid_and_empty_sizes_need_no_device():
     # null pointers with real work are rejected before any CUDA call
     assert lib.hgemm_launch(None, None, None, 4, 4, 4, 1.0, 0.0, None) == hg.HGEMM_ERR_INVALID_ARG
     assert hg.last_status() == hg.HGEMM_ERR_INVALID_ARG
+    # the host-buffer entry point checks the same before any CUDA call
+    assert lib.hgemm_launch_host(None, None, None, None, None, None, -1, 4, 4, 1.0, 0.0,
+                                 None) == hg.HGEMM_ERR_INVALID_ARG
+    assert lib.hgemm_launch_host(None, None, None, None, None, None, 0, 4, 4, 1.0, 0.0,
+                                 None) == hg.HGEMM_OK
+    assert lib.hgemm_launch_host(None, None, None, None, None, None, 4, 4, 4, 1.0, 0.0,
+                                 None) == hg.HGEMM_ERR_INVALID_ARG
 
 
 @pytest.mark.parametrize("M,nr", [(32768, 8), (4095, 8), (7, 3), (0, 2), (1, 4)])

@@ -84,6 +84,33 @@ def test_deterministic_bits(cuda, oracle):
     assert np.array_equal(r1.view(np.uint16), r2.view(np.uint16))
 
 
+@pytest.mark.parametrize("M,N,K,alpha,beta", [
+    (2304, 512, 256, 1.0, 0.0),   # two row blocks (1280 + 1024 rows)
+    (3000, 1000, 136, 1.5, 0.5),  # beta != 0: the C blocks are copied in too
+    (1100, 999, 72, 1.0, 0.25),   # N % 8 != 0: one block (B restrided once)
+    (8192, 256, 64, 1.0, 0.0),    # eight row blocks
+])
+def test_launch_host_pipelined_copies(cuda, oracle, M, N, K, alpha, beta):
+    """hgemm_launch_host: host (page-locked) A, B, C in and C out through caller-owned device
+    buffers, row blocks copied and computed in overlap; the result is the GEMM's, within the
+    parity bar against the fp64 oracle, and the device buffers hold the same C."""
+    A, B, C = _inputs(oracle, M, N, K, seed=M + N + K)
+    hA = torch.from_numpy(np.ascontiguousarray(A)).pin_memory()
+    hB = torch.from_numpy(np.ascontiguousarray(B)).pin_memory()
+    hC = torch.from_numpy(np.ascontiguousarray(C).copy()).pin_memory()
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    dC = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    s = torch.cuda.Stream()
+    cuda.launch_host(hA, hB, hC, dA, dB, dC, M, N, K, alpha, beta, s)
+    s.synchronize()
+    out = hC.numpy()
+    ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B, C, alpha, beta), K)
+    assert ok, worst
+    assert np.array_equal(out.view(np.uint16), host(dC).view(np.uint16))
+    assert cuda.device_status(clear=True)[0] == 0
+
+
 def test_tuned_launch_matches_default(cuda, oracle):
     M, N, K = 768, 640, 384
     A, B, C = _inputs(oracle, M, N, K, seed=8)
