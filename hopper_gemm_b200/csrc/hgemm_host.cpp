@@ -10,11 +10,12 @@
 // done. Copies in both directions and the math then overlap, and a call costs about the
 // host-to-device bytes at PCIe speed plus one block's GEMM and copy-out.
 //
-// Every block is an ordinary hgemm_launch on row-offset pointers, so each element of C gets
-// the same arithmetic as in a one-launch GEMM of the same tile. Row blocks start on multiples
-// of 256 rows (the pair tile height), which keeps every block's A and C pointers 16-byte
-// aligned. Shapes whose B or C need the restride copy (N % 8 != 0) run as one block so that
-// B is restrided once.
+// Every block is the GEMM of its rows on row-offset pointers with split-K ruled out, so each
+// element of C is summed in the same k order, and rounded the same way, as in one hgemm_launch
+// of the whole GEMM: the result is bit-identical to it. Problems that hgemm_launch itself would
+// split along K (a few tiles, long K) run as one block, and so do shapes whose B or C need the
+// restride copy (N % 8 != 0), so that B is restrided once. Row blocks start on multiples of 256
+// rows (the pair tile height), which keeps every block's A and C pointers 16-byte aligned.
 //
 // No counterpart in the reference (its solve() takes device pointers).
 
@@ -24,6 +25,14 @@
 #include <mutex>
 
 #include "hgemm_b200.h"
+
+// Defined in hgemm_sm100.cu, not part of the public header.
+extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_launch_unsplit(
+    const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M, int N, int K,
+    float alpha, float beta, hgemm_stream_t stream, int sm_limit);
+extern "C" __attribute__((visibility("hidden"))) int hgemm_internal_plan_current(
+    const hgemm_half_t *A, const hgemm_half_t *B, const hgemm_half_t *C, int M, int N, int K,
+    float beta, hgemm_plan_t *out);
 
 namespace {
 
@@ -82,7 +91,15 @@ extern "C" int hgemm_launch_host(const hgemm_half_t *A_h, const hgemm_half_t *B_
   if (!make_pipe(p)) return HGEMM_ERR_CUDA;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
-  const int nb = row_blocks(M, N);
+  int nb = row_blocks(M, N);
+  if (nb > 1) {
+    // One block when the whole GEMM would be split along K: row blocks could then not
+    // reproduce its summation order.
+    hgemm_plan_t whole;
+    if (hgemm_internal_plan_current(dA, dB, dC, M, N, K, beta, &whole) != HGEMM_OK ||
+        whole.ksplit > 1)
+      nb = 1;
+  }
   int bounds[kMaxBlocks + 1];
   {
     // Equal blocks rounded up to kBlockRowAlign rows; the last one takes the rest.
@@ -120,7 +137,9 @@ extern "C" int hgemm_launch_host(const hgemm_half_t *A_h, const hgemm_half_t *B_
     const int rows = bounds[i + 1] - bounds[i];
     chk(cudaStreamWaitEvent(s, p.blk_in[i], 0));
     if (rows > 0)
-      st = hgemm_launch(dA + r0 * K, dB, dC + r0 * N, rows, N, K, alpha, beta, stream);
+      st = nb == 1 ? hgemm_launch(dA, dB, dC, rows, N, K, alpha, beta, stream)
+                   : hgemm_internal_launch_unsplit(dA + r0 * K, dB, dC + r0 * N, rows, N, K,
+                                                   alpha, beta, stream, 0);
     chk(cudaEventRecord(p.blk_gemm[i], s));
     chk(cudaStreamWaitEvent(p.out, p.blk_gemm[i], 0));
     if (rows > 0)

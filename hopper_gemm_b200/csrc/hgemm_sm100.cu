@@ -2238,6 +2238,25 @@ __attribute__((visibility("hidden"))) int hgemm_internal_launch_unsplit(
                                 sm_limit > 0 ? sm_limit : 0, nullptr, 0, 1));
 }
 
+// The plan hgemm_launch would run on the current device for these operands (not part of the
+// public header; used by hgemm_launch_host to keep its row blocks on the one-launch
+// arithmetic).
+__attribute__((visibility("hidden"))) int hgemm_internal_plan_current(
+    const hgemm_half_t *A, const hgemm_half_t *B, const hgemm_half_t *C, int M, int N, int K,
+    float beta, hgemm_plan_t *out) {
+  if (!out) return HGEMM_ERR_INVALID_ARG;
+  int dev;
+  if (current_device(&dev) != HGEMM_OK) return HGEMM_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DevState *d = nullptr;
+  const int st = ensure_device(dev, &d);
+  if (st != HGEMM_OK) return st;
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+  return make_plan(M, N, K, beta, aligned16, 0, 0, 0, d->sm_count, d->pair_slots, out);
+}
+
 // Used by the multi-GPU layer only (not part of the public header). entry = 0: step-exit
 // barrier; entry = 1: step-entry barrier (every rank has entered the step).
 __attribute__((visibility("hidden"))) int hgemm_internal_peer_barrier(

@@ -104,8 +104,10 @@ size_t hgemm_noalloc_scratch_bytes(void);
  * landed, and each finished block of C is copied back to C_h while later blocks are still
  * being copied in and computed, so the transfers in both directions overlap the math.
  * Asynchronous: C_h holds the result once `stream` passes the call (the library's own copy
- * streams are joined back into it). Same semantics and status codes as hgemm_launch; a shape
- * with N % 8 != 0 runs as one block. Calls on one device are serialised on the host. */
+ * streams are joined back into it). Same semantics and status codes as hgemm_launch, and the
+ * same C bit for bit: the blocks never split K, and a problem that hgemm_launch would split
+ * along K, or one with N % 8 != 0, runs as one block. Calls on one device are serialised on
+ * the host. */
 int hgemm_launch_host(const hgemm_half_t *A_h, const hgemm_half_t *B_h, hgemm_half_t *C_h,
                       hgemm_half_t *dA, hgemm_half_t *dB, hgemm_half_t *dC, int M, int N, int K,
                       float alpha, float beta, hgemm_stream_t stream);

@@ -89,11 +89,14 @@ def test_deterministic_bits(cuda, oracle):
     (3000, 1000, 136, 1.5, 0.5),  # beta != 0: the C blocks are copied in too
     (1100, 999, 72, 1.0, 0.25),   # N % 8 != 0: one block (B restrided once)
     (8192, 256, 64, 1.0, 0.0),    # eight row blocks
+    (8192, 256, 1024, 1.0, 0.0),  # a 1024-row block alone would be split along K
+    (3072, 64, 4096, 1.0, 0.5),   # the whole GEMM is split along K (6 ways): one block
 ])
 def test_launch_host_pipelined_copies(cuda, oracle, M, N, K, alpha, beta):
     """hgemm_launch_host: host (page-locked) A, B, C in and C out through caller-owned device
     buffers, row blocks copied and computed in overlap; the result is the GEMM's, within the
-    parity bar against the fp64 oracle, and the device buffers hold the same C."""
+    parity bar against the fp64 oracle, the device buffers hold the same C, and that C is
+    bit-identical to one hgemm_launch of the whole GEMM on the same inputs."""
     A, B, C = _inputs(oracle, M, N, K, seed=M + N + K)
     hA = torch.from_numpy(np.ascontiguousarray(A)).pin_memory()
     hB = torch.from_numpy(np.ascontiguousarray(B)).pin_memory()
@@ -108,6 +111,10 @@ def test_launch_host_pipelined_copies(cuda, oracle, M, N, K, alpha, beta):
     ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B, C, alpha, beta), K)
     assert ok, worst
     assert np.array_equal(out.view(np.uint16), host(dC).view(np.uint16))
+    one = dev(C)
+    cuda.launch(dev(A), dev(B), one, M, N, K, alpha, beta)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.view(np.uint16), host(one).view(np.uint16))
     assert cuda.device_status(clear=True)[0] == 0
 
 
