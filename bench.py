@@ -93,6 +93,10 @@ def parse():
     ap.add_argument("--peer-standins", type=int, default=0,
                     help="with --grid: run the peer-store flavour of the fused multi-GPU path with "
                          "this many same-GPU buffers standing in for the peers' C (0-7)")
+    ap.add_argument("--grid-misalign", type=int, default=0,
+                    help="with --grid: start A, B and C this many halves past a 16-byte boundary "
+                         "(1-7): ours then restrides A and B and writes C with the SIMT-store "
+                         "epilogue, cuBLAS runs its own misaligned-operand kernels")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -332,16 +336,25 @@ def run_grid(args):
             subprocess.run([sys.executable, os.path.abspath(__file__), "--grid", "--grid-child",
                             "--grid-shapes", spec, "--grid-index", str(i),
                             "--grid-reps", str(args.grid_reps),
-                            "--peer-standins", str(args.peer_standins)], check=True)
+                            "--peer-standins", str(args.peer_standins),
+                            "--grid-misalign", str(args.grid_misalign)], check=True)
         return
     for i, (M, N, K, al, be) in enumerate(cases, start=args.grid_index):
-        A = hash_fill_(torch.empty((M, K), dtype=torch.float16, device=dev), 0x9E3779B9 ^ i)
-        B = hash_fill_(torch.empty((K, N), dtype=torch.float16, device=dev), 0x85EBCA6B ^ i)
-        C = hash_fill_(torch.empty((M, N), dtype=torch.float16, device=dev), 0x1234 ^ i)
-        R = C.clone()
-        C0 = C.clone()
-        T = C.clone()
-        use_cut = cut is not None and N % 8 == 0 and K % 8 == 0 and K > 0
+        off = args.grid_misalign
+
+        def mat(rows, cols):
+            # a rows x cols view that starts `off` halves into a fresh (256-byte aligned) buffer
+            return torch.empty(rows * cols + off, dtype=torch.float16, device=dev)[off:].view(
+                rows, cols)
+
+        A = hash_fill_(mat(M, K), 0x9E3779B9 ^ i)
+        B = hash_fill_(mat(K, N), 0x85EBCA6B ^ i)
+        C = hash_fill_(mat(M, N), 0x1234 ^ i)
+        R, C0, T = mat(M, N), mat(M, N), mat(M, N)
+        R.copy_(C)
+        C0.copy_(C)
+        T.copy_(C)
+        use_cut = cut is not None and N % 8 == 0 and K % 8 == 0 and K > 0 and off == 0
         # --peer-standins P: ours runs the fused multi-GPU path's peer-store kernel flavour
         # with P same-GPU buffers standing in for the peers' C (the SM-side cost of the peer
         # copies on one GPU, and a one-GPU target for profiling that kernel)
@@ -403,7 +416,7 @@ def run_grid(args):
             if use_cut:
                 tt.append(sample(ctl))
         fl = 2.0 * M * N * K
-        plan = hg.plan(M, N, K, beta=be)
+        plan = hg.plan(M, N, K, beta=be, aligned16=(off == 0))
         print(json.dumps({
             "shape": f"{M}x{N}x{K}", "alpha": al, "beta": be,
             "ours_tflops": fl / (statistics.median(to) * 1e-3) / 1e12,
@@ -414,6 +427,8 @@ def run_grid(args):
                                         if tt else None),
             "rel_l2_vs_cublas": l2, "rel_l2_vs_cutlass": l2t,
             "tile": f"{plan['tile_m']}x{plan['tile_n']}", "peer_standins": len(stand),
+            "path": {0: "none", 1: "tcgen05", 2: "scalar kernel"}[plan["path"]],
+            "misalign_halves": off,
             "restride": bool(plan["pad_a"] or plan["pad_b"])}), flush=True)
         del A, B, C, R, C0, T, stand
         torch.cuda.empty_cache()

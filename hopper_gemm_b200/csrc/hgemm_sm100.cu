@@ -1339,8 +1339,9 @@ __global__ void __launch_bounds__(TileCfg<PAIR, BN, EPIW>::THREADS, 1)
 }
 
 // ============================================================================ other kernels
-// Scalar fallback (misaligned pointers, K == 0): 64x64 output tile per block, 4x4 per
-// thread, fp32 accumulation in increasing k, same alpha/beta/rounding rules as above.
+// Scalar kernel (K == 0, and hgemm_launch_noalloc with a pointer off a 16-byte boundary):
+// 64x64 output tile per block, 4x4 per thread, fp32 accumulation in increasing k, same
+// alpha/beta/rounding rules as above.
 __global__ void __launch_bounds__(256) hgemm_simt_kernel(const __half *__restrict__ A,
                                                          const __half *__restrict__ B,
                                                          __half *__restrict__ C, int M, int N,
@@ -1763,6 +1764,14 @@ int ensure_device(int dev, DevState **out) {
 // ---------------------------------------------------------------- planning
 int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
+// Which of A, B, C start on a 16-byte boundary (bit 0, 1, 2), as make_plan takes it.
+constexpr unsigned kAllAligned = 7u;
+unsigned align_mask(const void *A, const void *B, const void *C) {
+  return (reinterpret_cast<uintptr_t>(A) % 16 == 0 ? 1u : 0u) |
+         (reinterpret_cast<uintptr_t>(B) % 16 == 0 ? 2u : 0u) |
+         (reinterpret_cast<uintptr_t>(C) % 16 == 0 ? 4u : 0u);
+}
+
 // Tile choice: the tile whose persistent schedule has the least per-CTA work on the
 // critical path (waves x columns per CTA), preferring the pair tiles, whose A+B traffic per
 // flop is the lowest. group_m keeps the concurrently running tiles' A and B blocks small
@@ -1781,7 +1790,8 @@ int choose_epi_warps(int tile, int kbn, float beta) {
   return kbn <= 2 ? 8 : 4;
 }
 
-int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int force_bn,
+// aligned: bit 0 / 1 / 2 set when A / B / C start on a 16-byte boundary (kAllAligned: all).
+int make_plan(int M, int N, int K, float beta, unsigned aligned, int force_bm, int force_bn,
               int group_m, int sm_count, int pair_slots, hgemm_plan_t *pl,
               bool persistent_only = false, int ksplit_req = 0) {
   std::memset(pl, 0, sizeof(*pl));
@@ -1797,7 +1807,7 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
     pl->path = 0;
     return HGEMM_OK;
   }
-  if (K == 0 || !aligned16) {
+  if (K == 0) {
     pl->path = 2;
     pl->tile_m = 64;
     pl->tile_n = 64;
@@ -1810,21 +1820,28 @@ int make_plan(int M, int N, int K, float beta, bool aligned16, int force_bm, int
   pl->path = 1;
   pl->lda = (K + 7) & ~7;
   pl->ldb = (N + 7) & ~7;
-  pl->pad_a = pl->lda != K;
-  pl->pad_b = pl->ldb != N;
+  // An operand whose base is not 16-byte aligned cannot be a TMA source either: it takes the
+  // same restride copy as a ragged one (the copy's loads handle any 2-byte offset). The
+  // reference sends such calls to its scalar fallback, which on B200 ran at 12-17 TFLOPS
+  // (1024^3, 4096^3) where cuBLAS on the same misaligned buffers ran at 68-167.
+  const bool a_al = (aligned & 1u) != 0, b_al = (aligned & 2u) != 0, c_al = (aligned & 4u) != 0;
+  pl->pad_a = pl->lda != K || !a_al;
+  pl->pad_b = pl->ldb != N || !b_al;
   // C with N % 8 != 0 has rows that TMA cannot address. With beta != 0 the GEMM runs on a
   // copy of C with a 16-byte row stride (restrided in, compacted back), two HBM-bound
   // passes instead of an epilogue of 2-byte loads and stores (B200: 4095^3 beta = 0.5
   // 374 -> 207 us, 8192x8191x8192 1634 -> 1032 us). With beta == 0 the compaction costs
   // more than the 2-byte stores save (4095^3: 162 us direct, 185 us padded), so those
-  // shapes keep the SIMT-store epilogue.
-  pl->pad_c = (N % 8 != 0) && beta != 0.0f;
+  // shapes keep the SIMT-store epilogue. A C that does not start on a 16-byte boundary is
+  // always written (and, with beta != 0, read) in place by the SIMT-store epilogue, whose
+  // 2-byte accesses need no alignment; the compaction's 16-byte stores would.
+  pl->pad_c = (N % 8 != 0) && beta != 0.0f && c_al;
   pl->ldc = pl->pad_c ? pl->ldb : N;
   pl->scratch_bytes = ((pl->pad_a ? static_cast<size_t>(M) * pl->lda : 0) +
                        (pl->pad_b ? static_cast<size_t>(K) * pl->ldb : 0) +
                        (pl->pad_c ? static_cast<size_t>(M) * pl->ldc : 0)) *
                       sizeof(__half);
-  pl->tma_store = (N % 8 == 0 || pl->pad_c) ? 1 : 0;
+  pl->tma_store = (c_al && (N % 8 == 0 || pl->pad_c)) ? 1 : 0;
 
   int tile = tile_from_force(force_bm, force_bn);
   if (tile < 0) {
@@ -2167,9 +2184,7 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
   DevState *d = nullptr;
   int st = ensure_device(dev, &d);
   if (st != HGEMM_OK) return st;
-  const bool aligned16 = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+  const unsigned aligned = align_mask(A, B, C);
   int sms = d->sm_count, pslots = d->pair_slots;
   if (sm_limit > 0 && sm_limit < sms) {
     sms = sm_limit;
@@ -2177,7 +2192,7 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
   }
   hgemm_plan_t pl;
   // Peer stores are issued by the tile's own epilogue, which split-K replaces.
-  st = make_plan(M, N, K, beta, aligned16, force_bm, force_bn, group_m, sms, pslots, &pl,
+  st = make_plan(M, N, K, beta, aligned, force_bm, force_bn, group_m, sms, pslots, &pl,
                  sm_limit > 0, npeers > 0 ? 1 : ksplit_req);
   if (st != HGEMM_OK) return st;
   if (pl.path == 0) return HGEMM_OK;
@@ -2188,7 +2203,7 @@ int launch_impl(const __half *A, const __half *B, __half *C, int M, int N, int K
     // 256x256 only). With the single 512-column accumulator that longer epilogue sits
     // between tiles; the double-buffered 256x256 tile hides it behind the next tile's main
     // loop (measured on 2 B200s: faster at K = 8192, slower at K = 16384).
-    st = make_plan(M, N, K, beta, aligned16, 256, 256, group_m, sms, pslots, &pl, sm_limit > 0,
+    st = make_plan(M, N, K, beta, aligned, 256, 256, group_m, sms, pslots, &pl, sm_limit > 0,
                    1);
     if (st != HGEMM_OK) return st;
   }
@@ -2251,10 +2266,8 @@ __attribute__((visibility("hidden"))) int hgemm_internal_plan_current(
   DevState *d = nullptr;
   const int st = ensure_device(dev, &d);
   if (st != HGEMM_OK) return st;
-  const bool aligned16 = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(C) % 16 == 0);
-  return make_plan(M, N, K, beta, aligned16, 0, 0, 0, d->sm_count, d->pair_slots, out);
+  return make_plan(M, N, K, beta, align_mask(A, B, C), 0, 0, 0, d->sm_count, d->pair_slots,
+                   out);
 }
 
 // Used by the multi-GPU layer only (not part of the public header). entry = 0: step-exit
@@ -2567,7 +2580,8 @@ void hgemm_release(void) {
 int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int force_bn,
                int group_m, int sm_count, int pair_slots, hgemm_plan_t *out) {
   if (!out) return HGEMM_ERR_INVALID_ARG;
-  return make_plan(M, N, K, beta, aligned16 != 0, force_bm, force_bn, group_m, sm_count,
+  return make_plan(M, N, K, beta, aligned16 != 0 ? kAllAligned : 0u, force_bm, force_bn, group_m,
+                   sm_count,
                    pair_slots, out);
 }
 
@@ -2628,14 +2642,15 @@ int launch_noalloc_impl(const __half *A, const __half *B, __half *C, int M, int 
   DevState *d = nullptr;
   int st = ensure_device(dev, &d);
   if (st != HGEMM_OK) return st;
-  const bool aligned16 = (reinterpret_cast<uintptr_t>(A) % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(B) % 16 == 0) &&
-                         (reinterpret_cast<uintptr_t>(C) % 16 == 0);
+  const unsigned aligned = align_mask(A, B, C);
   hgemm_plan_t pl;
-  st = make_plan(M, N, K, beta, aligned16, 0, 0, 0, d->sm_count, d->pair_slots, &pl);
+  st = make_plan(M, N, K, beta, aligned, 0, 0, 0, d->sm_count, d->pair_slots, &pl);
   if (st != HGEMM_OK) return st;
   if (pl.path == 0) return HGEMM_OK;
-  if (pl.path == 2) return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
+  // Operands that do not start on a 16-byte boundary would need their copies in the fixed
+  // array too; this entry point keeps them on the scalar kernel, which needs no scratch.
+  if (pl.path == 2 || aligned != kAllAligned)
+    return launch_simt(A, B, C, M, N, K, alpha, beta, stream);
   __half *w = nullptr;
   if (pl.pad_a || pl.pad_b || pl.pad_c) {
     if (pl.scratch_bytes > kNoallocScratchBytes) return HGEMM_ERR_TOO_LARGE;

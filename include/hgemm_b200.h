@@ -90,8 +90,9 @@ int hgemm_launch_tuned(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_
  * hgemm_release() after a device reset so that the address is looked up again. Each device has
  * its own copy of the array, and every call on a device shares that copy and leaves its
  * contents behind: two calls on one device that can overlap on the GPU (different streams)
- * race on it when both need restriding, so order them. Same arguments, semantics and status
- * codes as hgemm_launch. */
+ * race on it when both need restriding, so order them. Operands that do not start on a
+ * 16-byte boundary, which hgemm_launch copies like ragged ones, run here on the scalar kernel,
+ * which needs no scratch. Same arguments, semantics and status codes as hgemm_launch. */
 int hgemm_launch_noalloc(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half_t *C, int M,
                          int N, int K, float alpha, float beta, hgemm_stream_t stream);
 size_t hgemm_noalloc_scratch_bytes(void);
@@ -185,7 +186,7 @@ int hgemm_launch_splitk(const hgemm_half_t *A, const hgemm_half_t *B, hgemm_half
 
 /* Host-only description of what hgemm_launch_ex would run; needs no GPU. */
 typedef struct {
-  int path;       /* 0 no-op, 1 tcgen05 tiles, 2 SIMT fallback */
+  int path;       /* 0 no-op, 1 tcgen05 tiles, 2 scalar kernel (K == 0) */
   int tile_m;     /* rows per tile: 128 (one CTA) or 256 (2-SM pair) */
   int tile_n;     /* columns per tile */
   int pair;       /* 1 or 2 CTAs per UMMA */
@@ -195,9 +196,11 @@ typedef struct {
   int grid_ctas;  /* CTAs launched: with sched_static == 0 one cluster of `pair` CTAs per
                      tile, running clusters taking over not-yet-started ones (cluster launch
                      control); with sched_static == 1 one persistent cluster per slot */
-  int pad_a, pad_b;      /* operand restrided into scratch (K % 8, N % 8) */
+  int pad_a, pad_b;      /* operand restrided into scratch (K % 8 or N % 8 != 0, or a base that
+                            is not 16-byte aligned) */
   int lda, ldb;          /* leading dimensions the tensor maps use */
-  int tma_store;         /* 1: TMA-store epilogue; 0: SIMT stores (N % 8 != 0, beta == 0) */
+  int tma_store;         /* 1: TMA-store epilogue; 0: SIMT stores (N % 8 != 0 with beta == 0,
+                            or C not 16-byte aligned) */
   size_t scratch_bytes;  /* scratch needed for restrided operands */
   int sched_static;      /* 1: cluster c takes tiles c, c + clusters, ... (short tiles, or all
                             tiles co-resident); 0: cluster launch control */
@@ -209,8 +212,10 @@ typedef struct {
   int ldc;               /* row stride of the C the kernel writes */
 } hgemm_plan_t;
 
-/* `aligned16` says whether A, B and C all start on 16-byte boundaries; `sm_count` and
- * `pair_slots` (co-resident 2-CTA clusters) describe the device (<= 0: B200 defaults). */
+/* `aligned16` says whether A, B and C all start on 16-byte boundaries (0: the plan for three
+ * operands that do not, which restrides A and B and writes C with the SIMT-store epilogue);
+ * `sm_count` and `pair_slots` (co-resident 2-CTA clusters) describe the device (<= 0: B200
+ * defaults). */
 int hgemm_plan(int M, int N, int K, float beta, int aligned16, int force_bm, int force_bn,
                int group_m, int sm_count, int pair_slots, hgemm_plan_t *out);
 

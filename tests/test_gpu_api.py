@@ -46,7 +46,7 @@ def test_empty_m_or_n_is_noop(cuda):
     assert bool((C == 3.0).all())
 
 
-def test_misaligned_pointers_fall_back(cuda, oracle):
+def test_misaligned_pointers(cuda, oracle):
     M, N, K = 70, 90, 50
     A, B, C = _inputs(oracle, M, N, K, seed=4)
     bufA = torch.zeros(M * K + 1, dtype=torch.float16, device="cuda")
@@ -62,6 +62,35 @@ def test_misaligned_pointers_fall_back(cuda, oracle):
     out = host(bufC)[1:].reshape(M, N)
     ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B, C, 1.25, 0.75), K)
     assert ok, worst
+
+
+@pytest.mark.parametrize("M,N,K", [(70, 90, 50), (1000, 1024, 520), (777, 1001, 129)])
+@pytest.mark.parametrize("which", ["A", "B", "C", "ABC"])
+@pytest.mark.parametrize("off", [1, 3])
+def test_misaligned_operands_each(cuda, oracle, M, N, K, which, off):
+    """Operands that start `off` halves past a 16-byte boundary, one at a time and all three:
+    A and B go through the restride copy, C is read and written in place by the SIMT-store
+    epilogue. Every element vs fp64 at beta != 0 and at beta == 0 with NaN in C (never read),
+    and the halves just before and after C untouched."""
+    A, B, C = _inputs(oracle, M, N, K, seed=M + N + K + off)
+    for alpha, beta in ((1.25, 0.75), (1.0, 0.0)):
+        def place(x, shift):
+            buf = torch.full((x.size + shift + 8,), 7.0, dtype=torch.float16, device="cuda")
+            buf[shift:shift + x.size] = dev(x).view(-1)
+            return buf
+        sa, sb, sc = (off if w in which else 0 for w in "ABC")
+        Cin = C if beta != 0 else np.full_like(C, np.nan)
+        bA, bB, bC = place(A, sa), place(B, sb), place(Cin, sc)
+        cuda.launch(bA.data_ptr() + 2 * sa, bB.data_ptr() + 2 * sb, bC.data_ptr() + 2 * sc,
+                    M, N, K, alpha, beta)
+        torch.cuda.synchronize()
+        hb = host(bC)
+        out = hb[sc:sc + M * N].reshape(M, N)
+        ok, worst, _ = oracle.check(out, oracle.gemm_f64(A, B, C if beta != 0 else None,
+                                                        alpha, beta), K)
+        assert ok, (which, alpha, beta, worst)
+        assert np.all(hb[:sc] == 7.0) and np.all(hb[sc + M * N:] == 7.0)
+    assert cuda.device_status(clear=True)[0] == 0
 
 
 def test_side_stream_launch(cuda, oracle):

@@ -10,9 +10,17 @@ B200 = dict(sm_count=148, pair_slots=74)
 def test_noop_and_fallback_paths():
     assert hg.plan(0, 128, 64, **B200)["path"] == 0
     assert hg.plan(128, 0, 64, **B200)["path"] == 0
-    # K == 0 and misaligned pointers take the SIMT path (the reference's gemm_fallback route)
+    # K == 0 takes the scalar kernel (C = beta * C)
     assert hg.plan(128, 128, 0, **B200)["path"] == 2
-    assert hg.plan(128, 128, 64, aligned16=False, **B200)["path"] == 2
+    # pointers off a 16-byte boundary: A and B are restrided like ragged operands and C is
+    # written in place by the SIMT-store epilogue (beta != 0 too: no padded copy of C)
+    for beta in (0.0, 0.5):
+        for N in (128, 127):
+            p = hg.plan(128, N, 64, beta=beta, aligned16=False, **B200)
+            assert p["path"] == 1
+            assert (p["pad_a"], p["pad_b"], p["pad_c"], p["tma_store"]) == (1, 1, 0, 0)
+            assert p["ldc"] == N
+            assert p["scratch_bytes"] == 2 * (128 * p["lda"] + 64 * p["ldb"])
 
 
 @pytest.mark.parametrize("M,N,K,beta,pad_a,pad_b,pad_c,tma", [
