@@ -89,3 +89,33 @@ def test_noalloc_padded_c_counts_against_the_array(cuda):
     assert _call(lib.hgemm_launch_noalloc, A, B, C, M, N, K, 1.0, 0.0) == 0
     assert bool((C == float(K)).all())
     assert cuda.device_status(clear=True)[0] == 0
+
+
+def test_noalloc_misaligned_pointers_run_without_scratch(cuda, oracle):
+    """Pointers off a 16-byte boundary would need restride copies in the fixed array (8192^3:
+    256 MiB); the no-allocation entry point runs them on the scalar kernel instead, which needs
+    no scratch. Within the parity bar of the fp64 oracle and of hgemm_launch (which copies
+    them and stays on the tensor cores), two calls in a row."""
+    lib = cuda.lib
+    M, N, K = 1024, 1024, 1024
+    for call, (alpha, beta) in enumerate(((1.0, 0.5), (-1.5, 0.0))):
+        A, B, C = _inputs(oracle, M, N, K, seed=77 + call)
+
+        def placed(x):
+            buf = torch.zeros(x.size + 1, dtype=torch.float16, device="cuda")
+            buf[1:] = dev(x).view(-1)
+            return buf
+        bA, bB, bRef, bOut = placed(A), placed(B), placed(C), placed(C)
+        s = torch.cuda.current_stream().cuda_stream
+        args = (M, N, K, alpha, beta, s)
+        assert lib.hgemm_launch(bA.data_ptr() + 2, bB.data_ptr() + 2, bRef.data_ptr() + 2,
+                                *args) == 0
+        assert lib.hgemm_launch_noalloc(bA.data_ptr() + 2, bB.data_ptr() + 2,
+                                        bOut.data_ptr() + 2, *args) == 0
+        torch.cuda.synchronize()
+        ref, out = host(bRef)[1:].reshape(M, N), host(bOut)[1:].reshape(M, N)
+        fp64 = oracle.gemm_f64(A, B, C if beta != 0 else None, alpha, beta)
+        for got in (out, ref):
+            ok, worst, _ = oracle.check(got, fp64, K)
+            assert ok, (call, worst)
+    assert cuda.device_status(clear=True)[0] == 0
